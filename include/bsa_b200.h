@@ -1,0 +1,114 @@
+/*
+ * bsa_b200.h -- C ABI of the B200 block-sparse attention (BSA) engine.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (as void*), launches
+ * asynchronously on that stream and returns a status code (BSA_OK == 0).  Nothing here
+ * allocates device memory: outputs and scratch are owned by the caller.  Inputs are borrowed
+ * read-only.  The error message of the last failing call on the calling host thread is
+ * available from bsa_last_error().
+ *
+ * Tensor conventions (the reference's, longcat_video/models/block_sparse_attention.py):
+ *   q, k, v, out : [B, H, S, D] with element strides (sb, sh, ss) and d contiguous,
+ *                  S = T * Hl * Wl tokens in t-major (t, h, w) order (:74-76)
+ *   blocks       : chunk_thw = (cT, cH, cW) voxels, cT*cH*cW tokens each, numbered in
+ *                  (bt, bh, bw) block-major order (:98-104, :137-159).  A contiguous
+ *                  64-token block is shape (1, 1, S) with chunk (1, 1, 64).
+ *   pooled       : [B*H, nb, D] fp32, nb = S / (cT*cH*cW)
+ *   block index  : [B, H, nb, topk] int32, each row sorted ascending
+ */
+#ifndef BSA_B200_H
+#define BSA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define BSA_OK 0
+#define BSA_ERR_SHAPE 1       /* shape / chunk divisibility / size limits          */
+#define BSA_ERR_DTYPE 2       /* unsupported dtype for this entry point            */
+#define BSA_ERR_ALIGN 3       /* pointer or stride alignment (TMA needs 16 bytes)  */
+#define BSA_ERR_INDEX 4       /* block index out of range (device-side check)      */
+#define BSA_ERR_CUDA 5        /* CUDA runtime / driver error                       */
+#define BSA_ERR_TIMEOUT 6     /* a bounded device wait expired                     */
+#define BSA_ERR_ARG 7         /* null pointer / bad argument                       */
+
+/* dtype codes */
+#define BSA_DTYPE_F32 0
+#define BSA_DTYPE_F16 1
+#define BSA_DTYPE_BF16 2
+
+/* Library version (major*10000 + minor*100 + patch). */
+int bsa_version(void);
+
+/* Copies the last error message of this host thread into buf (NUL terminated); returns its
+ * length. */
+int bsa_last_error(char* buf, int n);
+
+/* Reads (and optionally clears) the sticky device-side error code written by the kernels
+ * (BSA_ERR_INDEX for an out-of-range block id, an internal wait-site code >= 100 for a
+ * bounded wait that expired).  Synchronises the device. */
+int bsa_device_error(int clear);
+
+/* mean_pool_blocks_3d -- longcat_video/models/block_sparse_attention.py:67-104.
+ * pooled[bh, blk, d] = mean over the block's tokens of x[b, h, token, d], in fp32 with a fixed
+ * fold-halves summation order (x[r] + x[r + n/2], recursively), n = cT*cH*cW (a power of two,
+ * at most 64).  With rope != NULL the 3-D RoPE of longcat_video/models/rope_3d.py:107-128 is
+ * applied first (fp32, rounded back to the input dtype, written to x_rot, contiguous
+ * [B,H,S,D]) and the rotated values are pooled.  rope holds per-axis tables, one angle per
+ * rotated pair, over the RoPE grid (rope_T, rope_H, rope_W) (token s at t = s / (H*W),
+ * h = (s / W) % H, w = s % W; this grid may differ from the block geometry, e.g. contiguous
+ * 64-token blocks over a 24x45x80 latent): cos_t[rope_T][dt/2], sin_t[rope_T][dt/2],
+ * cos_h[rope_H][dh/2], sin_h, cos_w[rope_W][dw/2], sin_w, concatenated in that order. */
+int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss,
+                  int T, int Hl, int Wl, int cT, int cH, int cW, const float* rope, int rope_dt, int rope_dh,
+                  int rope_dw, int rope_T, int rope_H, int rope_W, void* x_rot, float* pooled, void* stream);
+
+/* block_routing_scores + topk_block_indices -- block_sparse_attention.py:107-134.
+ * score[i][j] = fp32 fma chain over d = 0..D-1 of q_pooled[i][d] * k_pooled[j][d]; each row
+ * keeps the topk largest scores (ties: smaller block id first) and writes their block ids
+ * sorted ascending.  scores (nullable) receives the full [BH, nb, nb] score matrix instead of
+ * being kept on chip (only for small problems / the score API). */
+int bsa_score_topk(const float* q_pooled, const float* k_pooled, int BH, int nb, int D, int topk,
+                   int32_t* block_indices, float* scores, void* stream);
+
+/* block_routing_scores alone (block_sparse_attention.py:107-112): scores[BH, nq, nk] fp32. */
+int bsa_block_scores(const float* q_pooled, const float* k_pooled, int BH, int nq, int nk, int D, float* scores,
+                     void* stream);
+
+/* topk_block_indices on a given score matrix (block_sparse_attention.py:115-134): scores
+ * [rows, nk] fp32 -> block_indices [rows, topk], same selection rule as bsa_score_topk. */
+int bsa_topk_from_scores(const float* scores, int rows, int nk, int topk, int32_t* block_indices, void* stream);
+
+/* Sparse attention over given block indices -- the kernel-level entry of the reference
+ * (bsa_attention_metal*(q, k, v, block_indices, chunk_thw, shape),
+ * longcat_video/models/block_sparse_attention_metal.py:224-295, 484-548, 729-810, 985-1046).
+ * out[b,h,s,:] = softmax over the tokens of the selected KV blocks of s's block.
+ * dtype: BSA_DTYPE_F16 or BSA_DTYPE_BF16; D <= 128 and D % 8 == 0; block size 64.
+ * q/k/v strides: element strides of [B,H,S,D] (d contiguous); b and h must merge
+ * (sb == H*sh) unless B == 1.  Block ids are range-checked on the device. */
+int bsa_attention_indices(const void* q, const void* k, const void* v, const int32_t* block_indices, int dtype,
+                          int B, int H, int S, int D, const int64_t* q_strides, const int64_t* k_strides,
+                          const int64_t* v_strides, int T, int Hl, int Wl, int cT, int cH, int cW, int topk,
+                          float sm_scale, void* out, const int64_t* out_strides, void* stream);
+
+/* Full BSA call -- bsa_attention(q, k, v, shape, sparsity, chunk_thw, sm_scale),
+ * block_sparse_attention.py:201-250: pool Q and K, score, top-k, sparse attention.
+ * scratch: caller-provided device memory of bsa_forward_scratch_bytes() bytes (pooled fp32
+ * Q/K).  block_indices receives the routing ([B,H,nb,topk]).  With rope != NULL, q and k are
+ * pre-RoPE and q_rot / k_rot (contiguous [B,H,S,D]) receive the rotated tensors that the
+ * attention then reads. */
+int64_t bsa_forward_scratch_bytes(int B, int H, int S, int D, int cT, int cH, int cW);
+int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
+                const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl, int Wl,
+                int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt, int rope_dh,
+                int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot, void* scratch,
+                int32_t* block_indices, void* out, const int64_t* out_strides, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BSA_B200_H */

@@ -1,0 +1,269 @@
+// C ABI of the BSA engine (declared in include/bsa_b200.h): argument validation, TMA tensor-map
+// construction and kernel composition.  No entry point allocates device memory.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include "bsa_kernels.h"
+
+namespace {
+
+thread_local char g_msg[512] = {0};
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  return fail(BSA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int elt_bytes(int dtype) { return dtype == BSA_DTYPE_F32 ? 4 : 2; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Shared geometry checks of block_sparse_attention.py:86-96 (same wording as the reference).
+int check_geometry(int S, int T, int Hl, int Wl, int cT, int cH, int cW) {
+  if (cT <= 0 || cH <= 0 || cW <= 0 || T <= 0 || Hl <= 0 || Wl <= 0)
+    return fail(BSA_ERR_SHAPE, "shape and chunk_thw must be positive");
+  if (T % cT || Hl % cH || Wl % cW)
+    return fail(BSA_ERR_SHAPE,
+                "Latent shape (%d, %d, %d) must be a multiple of chunk_thw (%d, %d, %d); refinement padding should "
+                "guarantee this.",
+                T, Hl, Wl, cT, cH, cW);
+  if (static_cast<long long>(T) * Hl * Wl != S)
+    return fail(BSA_ERR_SHAPE, "S=%d doesn't match T*H*W=%lld for shape (%d, %d, %d)", S,
+                static_cast<long long>(T) * Hl * Wl, T, Hl, Wl);
+  return BSA_OK;
+}
+
+// 5-D tiled map over one of q/k/v: dims (d, w, h, t, b*h), box (64, cW, cH, cT, 1), 128B swizzle.
+// Out-of-range d (D < 128) reads as zero, which pads the head dimension for the MMA.
+int make_map(CUtensorMap* m, const void* base, int dtype, int B, int H, int D, const int64_t* st, int T, int Hl,
+             int Wl, int cT, int cH, int cW, const char* name) {
+  auto enc = encode_fn();
+  if (!enc) return fail(BSA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int e = elt_bytes(dtype);
+  const int64_t sb = st[0], sh = st[1], ss = st[2];
+  if (!aligned16(base)) return fail(BSA_ERR_ALIGN, "%s: base pointer must be 16-byte aligned", name);
+  if ((ss * e) % 16 || (sh * e) % 16 || (B > 1 && (sb * e) % 16))
+    return fail(BSA_ERR_ALIGN, "%s: strides must be multiples of 16 bytes (got sb=%lld sh=%lld ss=%lld elements)",
+                name, (long long)sb, (long long)sh, (long long)ss);
+  if (B > 1 && sb != static_cast<int64_t>(H) * sh)
+    return fail(BSA_ERR_SHAPE, "%s: batch and head strides must merge (sb == H*sh) when B > 1", name);
+  cuuint64_t dims[5] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(Wl), static_cast<cuuint64_t>(Hl),
+                        static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(B) * H};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(ss * e), static_cast<cuuint64_t>(ss * e * Wl),
+                           static_cast<cuuint64_t>(ss * e * Wl * Hl), static_cast<cuuint64_t>(sh * e)};
+  cuuint32_t box[5] = {64, static_cast<cuuint32_t>(cW), static_cast<cuuint32_t>(cH), static_cast<cuuint32_t>(cT), 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == BSA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = enc(m, dt, 5, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BSA_ERR_ARG, "%s: cuTensorMapEncodeTiled failed (%d)", name, static_cast<int>(r));
+  return BSA_OK;
+}
+
+int check_pool_args(const void* x, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss, int T,
+                    int Hl, int Wl, int cT, int cH, int cW, float* pooled) {
+  if (!x || !pooled) return fail(BSA_ERR_ARG, "null pointer");
+  if (dtype != BSA_DTYPE_F32 && dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
+    return fail(BSA_ERR_DTYPE, "unsupported dtype code %d", dtype);
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(BSA_ERR_SHAPE, "empty tensor");
+  int rc = check_geometry(S, T, Hl, Wl, cT, cH, cW);
+  if (rc) return rc;
+  const int n = cT * cH * cW;
+  if (n & (n - 1) || n > 64) return fail(BSA_ERR_SHAPE, "block size %d must be a power of two <= 64", n);
+  if (D % 8 || D > 128) return fail(BSA_ERR_SHAPE, "head_dim D=%d must be a multiple of 8 and <= 128", D);
+  const int e = elt_bytes(dtype);
+  if (!aligned16(x) || (ss * e) % 16 || (sh * e) % 16 || (sb * e) % 16)
+    return fail(BSA_ERR_ALIGN, "x must be 16-byte aligned with 16-byte-multiple strides");
+  return BSA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bsa_version(void) { return 100; }
+
+int bsa_last_error(char* buf, int n) {
+  const int len = static_cast<int>(strlen(g_msg));
+  if (buf && n > 0) {
+    strncpy(buf, g_msg, n - 1);
+    buf[n - 1] = 0;
+  }
+  return len;
+}
+
+int bsa_device_error(int clear) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return cuda_fail("cudaDeviceSynchronize");
+  const int a = bsa::attn_device_error(clear);
+  const int s = bsa::score_device_error(clear);
+  return a ? a : s;
+}
+
+int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss, int T,
+                  int Hl, int Wl, int cT, int cH, int cW, const float* rope, int rope_dt, int rope_dh, int rope_dw,
+                  int rope_T, int rope_H, int rope_W, void* x_rot, float* pooled, void* stream) {
+  int rc = check_pool_args(x, dtype, B, H, S, D, sb, sh, ss, T, Hl, Wl, cT, cH, cW, pooled);
+  if (rc) return rc;
+  if (rope) {
+    if (!x_rot) return fail(BSA_ERR_ARG, "x_rot is required with rope tables");
+    if (!aligned16(x_rot)) return fail(BSA_ERR_ALIGN, "x_rot must be 16-byte aligned");
+    if (rope_dt + rope_dh + rope_dw != D || (rope_dt | rope_dh | rope_dw) & 1)
+      return fail(BSA_ERR_SHAPE, "rope dims (%d, %d, %d) must be even and sum to D=%d", rope_dt, rope_dh, rope_dw, D);
+    if (static_cast<long long>(rope_T) * rope_H * rope_W != S)
+      return fail(BSA_ERR_SHAPE, "rope grid (%d, %d, %d) does not cover S=%d", rope_T, rope_H, rope_W, S);
+  }
+  bsa::PoolArgs a;
+  a.x = x; a.dtype = dtype; a.B = B; a.H = H; a.S = S; a.D = D; a.sb = sb; a.sh = sh; a.ss = ss;
+  a.T = T; a.Hl = Hl; a.Wl = Wl; a.cT = cT; a.cH = cH; a.cW = cW;
+  a.rope = rope; a.rope_dt = rope_dt; a.rope_dh = rope_dh; a.rope_dw = rope_dw;
+  a.rope_T = rope_T; a.rope_H = rope_H; a.rope_W = rope_W;
+  a.x_rot = x_rot; a.pooled = pooled;
+  rc = bsa::launch_pool(a, static_cast<cudaStream_t>(stream));
+  if (rc == BSA_ERR_CUDA) return cuda_fail("pool kernel launch");
+  if (rc) return fail(rc, "pool: unsupported configuration");
+  return BSA_OK;
+}
+
+int bsa_score_topk(const float* q_pooled, const float* k_pooled, int BH, int nb, int D, int topk,
+                   int32_t* block_indices, float* scores, void* stream) {
+  if (!q_pooled || !k_pooled || !block_indices) return fail(BSA_ERR_ARG, "null pointer");
+  if (BH <= 0 || nb <= 0 || D <= 0 || D > 128) return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nb=%d D=%d", BH, nb, D);
+  if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
+  bsa::ScoreArgs a;
+  a.qp = q_pooled; a.kp = k_pooled; a.BH = BH; a.nq = nb; a.nk = nb; a.D = D; a.topk = topk;
+  a.idx = block_indices; a.scores = scores; a.scores_in = nullptr;
+  const int rc = bsa::launch_score_topk(a, static_cast<cudaStream_t>(stream));
+  if (rc == BSA_ERR_CUDA) return cuda_fail("score/top-k kernel launch");
+  if (rc) return fail(rc, "score/top-k: %d KV blocks do not fit the on-chip score rows", nb);
+  return BSA_OK;
+}
+
+int bsa_block_scores(const float* q_pooled, const float* k_pooled, int BH, int nq, int nk, int D, float* scores,
+                     void* stream) {
+  if (!q_pooled || !k_pooled || !scores) return fail(BSA_ERR_ARG, "null pointer");
+  if (BH <= 0 || nq <= 0 || nk <= 0 || D <= 0 || D > 128)
+    return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nq=%d nk=%d D=%d", BH, nq, nk, D);
+  bsa::ScoreArgs a;
+  a.qp = q_pooled; a.kp = k_pooled; a.BH = BH; a.nq = nq; a.nk = nk; a.D = D; a.topk = 1;
+  a.idx = nullptr; a.scores = scores; a.scores_in = nullptr;
+  const int rc = bsa::launch_scores_only(a, static_cast<cudaStream_t>(stream));
+  if (rc == BSA_ERR_CUDA) return cuda_fail("score kernel launch");
+  if (rc) return fail(rc, "scores: %d KV blocks do not fit the on-chip score rows", nk);
+  return BSA_OK;
+}
+
+int bsa_topk_from_scores(const float* scores, int rows, int nk, int topk, int32_t* block_indices, void* stream) {
+  if (!scores || !block_indices) return fail(BSA_ERR_ARG, "null pointer");
+  if (rows <= 0 || nk <= 0) return fail(BSA_ERR_SHAPE, "bad sizes rows=%d nk=%d", rows, nk);
+  if (topk < 1 || topk > nk) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nk);
+  bsa::ScoreArgs a;
+  a.qp = nullptr; a.kp = nullptr; a.BH = 1; a.nq = rows; a.nk = nk; a.D = 1; a.topk = topk;
+  a.idx = block_indices; a.scores = nullptr; a.scores_in = scores;
+  const int rc = bsa::launch_score_topk(a, static_cast<cudaStream_t>(stream));
+  if (rc == BSA_ERR_CUDA) return cuda_fail("top-k kernel launch");
+  if (rc) return fail(rc, "top-k: %d KV blocks do not fit the on-chip score rows", nk);
+  return BSA_OK;
+}
+
+int bsa_attention_indices(const void* q, const void* k, const void* v, const int32_t* block_indices, int dtype,
+                          int B, int H, int S, int D, const int64_t* q_strides, const int64_t* k_strides,
+                          const int64_t* v_strides, int T, int Hl, int Wl, int cT, int cH, int cW, int topk,
+                          float sm_scale, void* out, const int64_t* out_strides, void* stream) {
+  if (!q || !k || !v || !block_indices || !out || !q_strides || !k_strides || !v_strides || !out_strides)
+    return fail(BSA_ERR_ARG, "null pointer");
+  if (dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
+    return fail(BSA_ERR_DTYPE, "sparse attention supports fp16 and bf16 inputs (dtype code %d)", dtype);
+  if (B <= 0 || H <= 0 || S <= 0) return fail(BSA_ERR_SHAPE, "empty tensor");
+  int rc = check_geometry(S, T, Hl, Wl, cT, cH, cW);
+  if (rc) return rc;
+  if (cT * cH * cW != 64)
+    return fail(BSA_ERR_SHAPE, "block size must be 64 tokens (chunk_thw product), got %d", cT * cH * cW);
+  if (D % 8 || D < 8 || D > 128) return fail(BSA_ERR_SHAPE, "head_dim D=%d must be a multiple of 8 in [8, 128]", D);
+  const int nb = S / 64;
+  if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
+  if (!aligned16(block_indices)) return fail(BSA_ERR_ALIGN, "block_indices must be 16-byte aligned");
+  CUtensorMap mq, mk, mv;
+  if ((rc = make_map(&mq, q, dtype, B, H, D, q_strides, T, Hl, Wl, cT, cH, cW, "q"))) return rc;
+  if ((rc = make_map(&mk, k, dtype, B, H, D, k_strides, T, Hl, Wl, cT, cH, cW, "k"))) return rc;
+  if ((rc = make_map(&mv, v, dtype, B, H, D, v_strides, T, Hl, Wl, cT, cH, cW, "v"))) return rc;
+  bsa::AttnArgs a;
+  a.idx = block_indices; a.out = out;
+  a.B = B; a.H = H; a.S = S; a.D = D; a.nb = nb; a.topk = topk;
+  a.Hl = Hl; a.Wl = Wl; a.cT = cT; a.cH = cH; a.cW = cW;
+  a.out_sb = out_strides[0]; a.out_sh = out_strides[1]; a.out_ss = out_strides[2];
+  a.sm_scale = sm_scale;
+  a.is_bf16 = dtype == BSA_DTYPE_BF16;
+  rc = bsa::launch_attn(&mq, &mk, &mv, a, static_cast<cudaStream_t>(stream));
+  if (rc == BSA_ERR_CUDA) return cuda_fail("attention kernel launch");
+  return rc;
+}
+
+int64_t bsa_forward_scratch_bytes(int B, int H, int S, int D, int cT, int cH, int cW) {
+  const int n = cT * cH * cW;
+  if (n <= 0 || B <= 0 || H <= 0 || S <= 0 || D <= 0) return 0;
+  return 2ll * B * H * (S / n) * D * 4;
+}
+
+int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
+                const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl, int Wl,
+                int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt, int rope_dh,
+                int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot, void* scratch,
+                int32_t* block_indices, void* out, const int64_t* out_strides, void* stream) {
+  if (!scratch || !q_strides || !k_strides || !v_strides) return fail(BSA_ERR_ARG, "null pointer");
+  if (!aligned16(scratch)) return fail(BSA_ERR_ALIGN, "scratch must be 16-byte aligned");
+  if (dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
+    return fail(BSA_ERR_DTYPE, "sparse attention supports fp16 and bf16 inputs (dtype code %d)", dtype);
+  const int n = cT * cH * cW;
+  if (n != 64) {
+    int rc = check_geometry(S, T, Hl, Wl, cT, cH, cW);
+    if (rc) return rc;
+    return fail(BSA_ERR_SHAPE, "block size must be 64 tokens (chunk_thw product), got %d", n);
+  }
+  const int nb = S / 64;
+  float* qp = static_cast<float*>(scratch);
+  float* kp = qp + static_cast<int64_t>(B) * H * nb * D;
+  int rc = bsa_mean_pool(q, dtype, B, H, S, D, q_strides[0], q_strides[1], q_strides[2], T, Hl, Wl, cT, cH, cW, rope,
+                         rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, q_rot, qp, stream);
+  if (rc) return rc;
+  rc = bsa_mean_pool(k, dtype, B, H, S, D, k_strides[0], k_strides[1], k_strides[2], T, Hl, Wl, cT, cH, cW, rope,
+                     rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, k_rot, kp, stream);
+  if (rc) return rc;
+  rc = bsa_score_topk(qp, kp, B * H, nb, D, topk, block_indices, nullptr, stream);
+  if (rc) return rc;
+  if (rope) {
+    const int64_t cst[3] = {static_cast<int64_t>(H) * S * D, static_cast<int64_t>(S) * D, D};
+    return bsa_attention_indices(q_rot, k_rot, v, block_indices, dtype, B, H, S, D, cst, cst, v_strides, T, Hl, Wl,
+                                 cT, cH, cW, topk, sm_scale, out, out_strides, stream);
+  }
+  return bsa_attention_indices(q, k, v, block_indices, dtype, B, H, S, D, q_strides, k_strides, v_strides, T, Hl,
+                               Wl, cT, cH, cW, topk, sm_scale, out, out_strides, stream);
+}
+
+}  // extern "C"

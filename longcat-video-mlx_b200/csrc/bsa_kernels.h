@@ -1,0 +1,53 @@
+// Internal interface between the C-ABI layer (bsa_capi.cu) and the kernels.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "../../include/bsa_b200.h"
+
+namespace bsa {
+
+// ------------------------------------------------------------------ pooling (+ fused RoPE)
+struct PoolArgs {
+  const void* x;         // [B,H,S,D] with strides sb, sh, ss (elements), d contiguous
+  int dtype;             // BSA_DTYPE_*
+  int B, H, S, D;
+  long long sb, sh, ss;
+  int T, Hl, Wl, cT, cH, cW;
+  // optional fused 3-D RoPE (rope_3d.py:107-128): per-axis tables, fp32, one entry per pair
+  const float* rope;     // nullable: [cos_t | sin_t | cos_h | sin_h | cos_w | sin_w]
+  int rope_dt, rope_dh, rope_dw;
+  int rope_T, rope_H, rope_W;  // RoPE grid; token s sits at (s / (H*W), (s / W) % H, s % W)
+  void* x_rot;           // [B,H,S,D] contiguous, same dtype as x (required when rope != null)
+  float* pooled;         // [B*H, nb, D] fp32
+};
+int launch_pool(const PoolArgs& a, cudaStream_t stream);
+
+// ------------------------------------------------------------------ block scores + top-k
+struct ScoreArgs {
+  const float* qp;       // [BH, nb, D] fp32
+  const float* kp;       // [BH, nk, D] fp32
+  int BH, nq, nk, D, topk;
+  int32_t* idx;          // [BH, nb, topk], ascending block ids
+  float* scores;         // nullable: [BH, nq, nk] fp32 output (routing-score API)
+  const float* scores_in;  // nullable: select from these scores instead of computing them
+};
+int launch_score_topk(const ScoreArgs& a, cudaStream_t stream);
+int launch_scores_only(const ScoreArgs& a, cudaStream_t stream);
+
+// ------------------------------------------------------------------ sparse attention
+struct AttnArgs {
+  const int32_t* idx;
+  void* out;
+  int B, H, S, D, nb, topk;
+  int Hl, Wl, cT, cH, cW;
+  long long out_sb, out_sh, out_ss;
+  float sm_scale;
+  int is_bf16;
+};
+int launch_attn(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, const AttnArgs& a,
+                cudaStream_t stream);
+int attn_device_error(int clear);
+int score_device_error(int clear);
+
+}  // namespace bsa

@@ -1,0 +1,270 @@
+"""ctypes binding of the engine's C ABI (include/bsa_b200.h) for torch CUDA tensors.
+
+The shared library is built in-tree by ``longcat-video-mlx_b200/build.py``.  There is no
+fallback: if the library is missing or no CUDA device is present, every compute entry point
+raises.  Shape / dtype / alignment errors come back as ``ValueError`` with the C layer's
+message (the reference raises ``ValueError`` for the same conditions,
+``block_sparse_attention.py:86-96`` and ``block_sparse_attention_metal.py:248-262``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libbsa_b200.so")
+
+BSA_OK = 0
+BSA_ERR_SHAPE = 1
+BSA_ERR_DTYPE = 2
+BSA_ERR_ALIGN = 3
+BSA_ERR_INDEX = 4
+BSA_ERR_CUDA = 5
+BSA_ERR_TIMEOUT = 6
+BSA_ERR_ARG = 7
+
+DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+_lib = None
+_lock = threading.Lock()
+
+_c_i64p = ctypes.POINTER(ctypes.c_int64)
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_f = ctypes.c_float
+
+_SIGNATURES = {
+    "bsa_version": ([], _i),
+    "bsa_last_error": ([ctypes.c_char_p, _i], _i),
+    "bsa_device_error": ([_i], _i),
+    "bsa_mean_pool": ([_vp, _i, _i, _i, _i, _i, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _i, _i, _i, _i, _i, _i,
+                       _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp], _i),
+    "bsa_score_topk": ([_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp], _i),
+    "bsa_block_scores": ([_vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
+    "bsa_topk_from_scores": ([_vp, _i, _i, _i, _vp, _vp], _i),
+    "bsa_attention_indices": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i, _i,
+                               _i, _i, _f, _vp, _c_i64p, _vp], _i),
+    "bsa_forward_scratch_bytes": ([_i, _i, _i, _i, _i, _i, _i], ctypes.c_int64),
+    "bsa_forward": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i, _i, _i, _i, _f,
+                     _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _c_i64p, _vp], _i),
+}
+
+
+class BSAError(RuntimeError):
+    """A CUDA-side failure of the BSA engine (launch error, device error flag)."""
+
+
+def library_loaded() -> bool:
+    return _lib is not None
+
+
+def lib():
+    """Load the engine library once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise BSAError(
+                    f"BSA CUDA library not found at {LIB_PATH}; build it with "
+                    "`python longcat-video-mlx_b200/build.py` (there is no CPU fallback)")
+            handle = ctypes.CDLL(LIB_PATH)
+            for name, (args, res) in _SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.argtypes = args
+                fn.restype = res
+            _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(512)
+    lib().bsa_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def _check(rc: int, what: str) -> None:
+    if rc == BSA_OK:
+        return
+    msg = last_error()
+    if rc in (BSA_ERR_SHAPE, BSA_ERR_DTYPE, BSA_ERR_ALIGN, BSA_ERR_ARG):
+        raise ValueError(msg or f"{what}: invalid argument (code {rc})")
+    raise BSAError(f"{what} failed (code {rc}): {msg}")
+
+
+def device_error(clear: bool = True) -> int:
+    """Sticky device-side error code (0 = none); synchronises the device."""
+    return int(lib().bsa_device_error(1 if clear else 0))
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not isinstance(t, torch.Tensor):
+            raise TypeError("expected torch tensors")
+        if not t.is_cuda:
+            raise ValueError("BSA engine inputs must be CUDA tensors (there is no CPU path)")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _strides(t: torch.Tensor):
+    if t.stride(-1) != 1:
+        raise ValueError("the last (head_dim) axis must be contiguous")
+    arr = (ctypes.c_int64 * 3)(t.stride(0), t.stride(1), t.stride(2))
+    return arr
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}") from None
+
+
+def _geometry(S: int, shape: Sequence[int], chunk_thw: Sequence[int]):
+    T, H_, W = (int(v) for v in shape)
+    cT, cH, cW = (int(v) for v in chunk_thw)
+    if T % cT or H_ % cH or W % cW:
+        raise ValueError(
+            f"Latent shape ({T}, {H_}, {W}) must be a multiple of "
+            f"chunk_thw {tuple(chunk_thw)}; refinement padding should guarantee this.")
+    if S != T * H_ * W:
+        raise ValueError(f"S={S} doesn't match T*H*W={T * H_ * W} for shape {tuple(shape)}")
+    return T, H_, W, cT, cH, cW
+
+
+# ------------------------------------------------------------------------------------ ops
+def mean_pool(x: torch.Tensor, shape, chunk_thw, rope: Optional[Tuple] = None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """fp32 block means [B, H, nb, D]; with ``rope=(tables, dims, grid)`` also the rotated x."""
+    _require_cuda(x)
+    if x.dim() != 4:
+        raise ValueError("expected x of shape [B, H, S, D]")
+    B, H, S, D = x.shape
+    T, H_, W, cT, cH, cW = _geometry(S, shape, chunk_thw)
+    nb = S // (cT * cH * cW)
+    pooled = torch.empty((B, H, nb, D), device=x.device, dtype=torch.float32)
+    st = _strides(x)
+    x_rot = None
+    rope_ptr, rdims, rgrid = None, (0, 0, 0), (0, 0, 0)
+    if rope is not None:
+        tables, rdims, rgrid = rope
+        x_rot = torch.empty((B, H, S, D), device=x.device, dtype=x.dtype)
+        rope_ptr = tables.data_ptr()
+    rc = lib().bsa_mean_pool(x.data_ptr(), _dtype_code(x), B, H, S, D, st[0], st[1], st[2], T, H_, W, cT, cH, cW,
+                             rope_ptr, rdims[0], rdims[1], rdims[2], rgrid[0], rgrid[1], rgrid[2],
+                             x_rot.data_ptr() if x_rot is not None else None, pooled.data_ptr(), _stream(x))
+    _check(rc, "bsa_mean_pool")
+    return pooled, x_rot
+
+
+def score_topk(qp: torch.Tensor, kp: torch.Tensor, topk: int, return_scores: bool = False):
+    """Block scores + per-row top-k.  qp, kp: [B, H, nb, D] fp32 contiguous."""
+    _require_cuda(qp, kp)
+    if qp.dtype != torch.float32 or kp.dtype != torch.float32:
+        raise ValueError("pooled blocks must be fp32")
+    qp = qp.contiguous()
+    kp = kp.contiguous()
+    B, H, nb, D = qp.shape
+    if kp.shape != qp.shape:
+        raise ValueError("q and k block tensors must have the same shape for top-k routing")
+    idx = torch.empty((B, H, nb, topk), device=qp.device, dtype=torch.int32)
+    scores = torch.empty((B, H, nb, nb), device=qp.device, dtype=torch.float32) if return_scores else None
+    rc = lib().bsa_score_topk(qp.data_ptr(), kp.data_ptr(), B * H, nb, D, int(topk), idx.data_ptr(),
+                              scores.data_ptr() if scores is not None else None, _stream(qp))
+    _check(rc, "bsa_score_topk")
+    return idx, scores
+
+
+def topk_from_scores(score: torch.Tensor, topk: int) -> torch.Tensor:
+    """[..., nq, nk] fp32 scores -> [..., nq, topk] int32 ascending block ids."""
+    _require_cuda(score)
+    s = score.to(torch.float32).contiguous()
+    nk = s.shape[-1]
+    rows = s.numel() // nk if nk else 0
+    idx = torch.empty((*s.shape[:-1], int(topk)), device=s.device, dtype=torch.int32)
+    rc = lib().bsa_topk_from_scores(s.data_ptr(), rows, nk, int(topk), idx.data_ptr(), _stream(s))
+    _check(rc, "bsa_topk_from_scores")
+    return idx
+
+
+def block_scores(qp: torch.Tensor, kp: torch.Tensor) -> torch.Tensor:
+    _require_cuda(qp, kp)
+    qp = qp.to(torch.float32).contiguous()
+    kp = kp.to(torch.float32).contiguous()
+    *lead, nq, D = qp.shape
+    nk = kp.shape[-2]
+    BH = 1
+    for v in lead:
+        BH *= int(v)
+    out = torch.empty((*lead, nq, nk), device=qp.device, dtype=torch.float32)
+    rc = lib().bsa_block_scores(qp.data_ptr(), kp.data_ptr(), BH, nq, nk, D, out.data_ptr(), _stream(qp))
+    _check(rc, "bsa_block_scores")
+    return out
+
+
+def attention_indices(q, k, v, block_indices, shape, chunk_thw, sm_scale: float,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _require_cuda(q, k, v, block_indices)
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("q, k, v must have the same shape [B, H, S, D]")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k, v must share one dtype")
+    B, H, S, D = q.shape
+    T, H_, W, cT, cH, cW = _geometry(S, shape, chunk_thw)
+    bi = block_indices
+    if bi.dtype != torch.int32:
+        bi = bi.to(torch.int32)
+    bi = bi.contiguous()
+    nb = S // (cT * cH * cW)
+    if bi.dim() != 4 or tuple(bi.shape[:3]) != (B, H, nb):
+        raise ValueError(f"block_indices must be [B, H, {nb}, top_k], got {tuple(bi.shape)}")
+    if out is None:
+        out = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
+    rc = lib().bsa_attention_indices(q.data_ptr(), k.data_ptr(), v.data_ptr(), bi.data_ptr(), _dtype_code(q), B, H, S,
+                                     D, _strides(q), _strides(k), _strides(v), T, H_, W, cT, cH, cW, int(bi.shape[-1]),
+                                     float(sm_scale), out.data_ptr(), _strides(out), _stream(q))
+    _check(rc, "bsa_attention_indices")
+    return out
+
+
+def forward(q, k, v, shape, chunk_thw, topk: int, sm_scale: float, rope: Optional[Tuple] = None,
+            out: Optional[torch.Tensor] = None, block_indices: Optional[torch.Tensor] = None,
+            scratch: Optional[torch.Tensor] = None):
+    """Full BSA call (pool -> score -> top-k -> sparse attention).  Returns (out, block_indices)."""
+    _require_cuda(q, k, v)
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("q, k, v must have the same shape [B, H, S, D]")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k, v must share one dtype")
+    B, H, S, D = q.shape
+    T, H_, W, cT, cH, cW = _geometry(S, shape, chunk_thw)
+    nb = S // (cT * cH * cW)
+    if out is None:
+        out = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
+    if block_indices is None:
+        block_indices = torch.empty((B, H, nb, int(topk)), device=q.device, dtype=torch.int32)
+    nbytes = int(lib().bsa_forward_scratch_bytes(B, H, S, D, cT, cH, cW))
+    if scratch is None or scratch.numel() * scratch.element_size() < nbytes:
+        scratch = torch.empty((max(nbytes, 16),), device=q.device, dtype=torch.uint8)
+    rope_ptr, rdims, rgrid = None, (0, 0, 0), (0, 0, 0)
+    q_rot = k_rot = None
+    if rope is not None:
+        tables, rdims, rgrid = rope
+        rope_ptr = tables.data_ptr()
+        q_rot = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
+        k_rot = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
+    rc = lib().bsa_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype_code(q), B, H, S, D, _strides(q),
+                           _strides(k), _strides(v), T, H_, W, cT, cH, cW, int(topk), float(sm_scale), rope_ptr,
+                           rdims[0], rdims[1], rdims[2], rgrid[0], rgrid[1], rgrid[2],
+                           q_rot.data_ptr() if q_rot is not None else None,
+                           k_rot.data_ptr() if k_rot is not None else None, scratch.data_ptr(),
+                           block_indices.data_ptr(), out.data_ptr(), _strides(out), _stream(q))
+    _check(rc, "bsa_forward")
+    return out, block_indices

@@ -1,0 +1,98 @@
+"""DiT visual self-attention with the BSA hook (xocialize/longcat-video-mlx
+``longcat_video/models/attention.py:35-275``), in torch, with the hook routed to the B200 engine.
+
+Only what the BSA path needs is here: QKV projection, fp32 RMSNorm on q/k (blocks.py:55-73),
+3-D RoPE, ``_process_attn`` (the hook, :71-179) and the output projection.  Every BSA backend
+name the reference accepts routes to the one CUDA engine; the hook's own fallback -- a
+``ValueError`` from BSA (shape not a multiple of chunk_thw) falls back to dense attention
+(:174-179) -- is kept as the reference has it.  With BSA on, RoPE is fused into the routing
+kernel instead of being applied as a separate pass.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from .block_sparse_attention import bsa_attention
+from .rope_3d import RotaryPositionalEmbedding
+
+BSA_BACKENDS = ("tier_a", "metal", "metal_v2", "metal_v3", "metal_v4", "cuda")
+
+
+class RMSNorm_FP32(torch.nn.Module):
+    """blocks.py:55-73: fp32 RMS normalisation, weight applied in the input dtype."""
+
+    def __init__(self, dim: int, eps: float):
+        super().__init__()
+        self.eps = eps
+        self.weight = torch.nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        norm = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+        return norm.to(x.dtype) * self.weight.to(x.dtype)
+
+
+class Attention(torch.nn.Module):
+    def __init__(self, dim: int, num_heads: int):
+        super().__init__()
+        assert dim % num_heads == 0, "dim must be divisible by num_heads"
+        self.dim = dim
+        self.num_heads = num_heads
+        self.head_dim = dim // num_heads
+        self.scale = self.head_dim ** -0.5
+        self.qkv = torch.nn.Linear(dim, dim * 3, bias=True)
+        self.q_norm = RMSNorm_FP32(self.head_dim, eps=1e-6)
+        self.k_norm = RMSNorm_FP32(self.head_dim, eps=1e-6)
+        self.proj = torch.nn.Linear(dim, dim)
+        self.rope_3d = RotaryPositionalEmbedding(self.head_dim)
+        # attention.py:62-69 defaults
+        self.enable_bsa: bool = False
+        self.bsa_sparsity: float = 0.9375
+        self.bsa_chunk_thw: Tuple[int, int, int] = (4, 4, 4)
+        self.bsa_backend: str = "tier_a"
+        self.bsa_topk: Optional[int] = None  # explicit k overrides the floor rule
+
+    def _bsa_ok(self, q: torch.Tensor, k: torch.Tensor, shape) -> bool:
+        return self.enable_bsa and shape is not None and q.shape[-2] == k.shape[-2]
+
+    def _process_attn(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      shape: Optional[Tuple[int, int, int]] = None, rope_grid=None) -> torch.Tensor:
+        """attention.py:71-179.  q, k, v: [B, H, S, D].  With ``rope_grid`` set, q and k are
+        pre-RoPE: the BSA path fuses the rotation, the dense path applies it first."""
+        if self._bsa_ok(q, k, shape):
+            try:
+                rope = self.rope_3d.tables(rope_grid, q.device) if rope_grid is not None else None
+                return bsa_attention(q, k, v, shape=shape, sparsity=self.bsa_sparsity,
+                                     chunk_thw=self.bsa_chunk_thw, sm_scale=self.scale, topk=self.bsa_topk,
+                                     rope=rope)
+            except ValueError:
+                # shape not a multiple of chunk_thw (or outside the kernel's limits): the
+                # reference falls back to dense attention here (attention.py:174-179)
+                pass
+        if rope_grid is not None:
+            q, k = self.rope_3d(q, k, rope_grid)
+        return F.scaled_dot_product_attention(q, k, v, scale=self.scale)
+
+    def forward(self, x: torch.Tensor, shape: Tuple[int, int, int],
+                num_cond_latents: Optional[int] = None) -> torch.Tensor:
+        """attention.py:181-233.  x: [B, N, C] -> [B, N, C]."""
+        B, N, C = x.shape
+        qkv = self.qkv(x).reshape(B, N, 3, self.num_heads, self.head_dim).permute(2, 0, 3, 1, 4)
+        q, k, v = qkv[0], qkv[1], qkv[2]
+        q = self.q_norm(q)
+        k = self.k_norm(k)
+        if num_cond_latents is not None and num_cond_latents > 0:
+            q, k = self.rope_3d(q, k, shape)
+            ncl = num_cond_latents * (N // shape[0])
+            cond_shape = (num_cond_latents, shape[1], shape[2])
+            x_cond = self._process_attn(q[:, :, :ncl], k[:, :, :ncl], v[:, :, :ncl], shape=cond_shape)
+            x_noise = self._process_attn(q[:, :, ncl:], k, v, shape=None)
+            out = torch.cat([x_cond, x_noise], dim=2)
+        else:
+            out = self._process_attn(q, k, v, shape=shape, rope_grid=shape)
+        out = out.transpose(1, 2).reshape(B, N, C)
+        return self.proj(out)

@@ -1,0 +1,331 @@
+"""GPU parity of the CUDA engine against the CPU oracle (oracle/bsa_oracle.py).
+
+Contract: block indices bit-exact wherever the fp32 pooled scores are
+computed identically (the engine and the oracle use the same fixed fp32 orders, so pooled means
+and scores must match bit for bit); attention outputs within relative L2 <= 1e-2 and max-abs
+<= 2e-2 of the fp32/fp64 oracle.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import bsa_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-2
+MAX_ABS = 2e-2
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()
+
+
+def _rand(shape, dtype, seed, device, scale=1.0):
+    g = torch.Generator(device="cpu")
+    g.manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(dtype).to(device)
+
+
+def _close(out: np.ndarray, ref: np.ndarray):
+    rel = np.linalg.norm(out - ref) / max(np.linalg.norm(ref), 1e-30)
+    mx = np.abs(out - ref).max()
+    assert rel <= REL_L2 and mx <= MAX_ABS, f"rel_l2={rel:.3e} max_abs={mx:.3e}"
+    return rel, mx
+
+
+GEOMS = [((4, 8, 8), (4, 4, 4)), ((1, 1, 1024), (1, 1, 64)), ((8, 4, 16), (2, 4, 8))]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("geom", GEOMS)
+def test_pool_bitexact(cuda, dtype, geom):
+    from longcat_video.models.block_sparse_attention import mean_pool_blocks_3d
+
+    shape, chunk = geom
+    S = shape[0] * shape[1] * shape[2]
+    x = _rand((2, 3, S, 128), dtype, 1, cuda)
+    got = mean_pool_blocks_3d(x, shape, chunk)
+    ref = orc.mean_pool_blocks_3d(_np(x), shape, chunk)
+    assert got.dtype == torch.float32
+    assert _np(got).tobytes() == ref.tobytes()
+
+
+def test_pool_strided_input_bitexact(cuda):
+    # q/k/v as produced by the DiT: reshape(B, N, 3, H, D).permute(2, 0, 3, 1, 4)
+    from longcat_video.models.block_sparse_attention import mean_pool_blocks_3d
+
+    B, N, H, D = 1, 512, 4, 64
+    qkv = _rand((B, N, 3, H, D), torch.bfloat16, 2, cuda).permute(2, 0, 3, 1, 4)
+    q = qkv[0]
+    assert not q.is_contiguous()
+    got = mean_pool_blocks_3d(q, (8, 8, 8), (4, 4, 4))
+    ref = orc.mean_pool_blocks_3d(_np(q), (8, 8, 8), (4, 4, 4))
+    assert _np(got).tobytes() == ref.tobytes()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_pool_fused_rope_bitexact(cuda, dtype):
+    from longcat_video import _native
+    from longcat_video.models.rope_3d import RopeTables
+
+    grid = (4, 6, 8)
+    S = 192
+    x = _rand((1, 2, S, 128), dtype, 3, cuda)
+    rt = RopeTables(grid, 128, cuda)
+    # product and oracle tables must be the same numbers
+    tabs = orc.rope_axis_tables(grid, 128)
+    assert np.array_equal(rt.host, np.concatenate([np.concatenate([c.ravel(), s.ravel()]) for c, s in tabs]))
+    pooled, x_rot = _native.mean_pool(x, (1, 1, S), (1, 1, 64), rope=rt.native_args())
+    cos, sin = orc.rope_full_tables(grid, 128)
+    ref_rot = orc.apply_rope(_np(x), cos, sin, "bf16" if dtype == torch.bfloat16 else "fp16")
+    assert _np(x_rot).tobytes() == ref_rot.tobytes()
+    ref_pool = orc.mean_pool_blocks_3d(ref_rot, (1, 1, S), (1, 1, 64))
+    assert _np(pooled).tobytes() == ref_pool.tobytes()
+
+
+@pytest.mark.parametrize("nb,D,k", [(64, 128, 4), (130, 128, 9), (200, 64, 1), (96, 40, 96), (1350, 128, 85)])
+def test_score_topk_bitexact(cuda, nb, D, k):
+    from longcat_video import _native
+
+    qp = _rand((1, 2, nb, D), torch.float32, 4, cuda)
+    kp = _rand((1, 2, nb, D), torch.float32, 5, cuda)
+    idx, scores = _native.score_topk(qp, kp, k, return_scores=True)
+    ref_s = orc.block_routing_scores(_np(qp), _np(kp))
+    assert _np(scores).tobytes() == ref_s.tobytes()
+    ref_i, _ = orc.topk_block_indices(ref_s, topk=k)
+    assert np.array_equal(idx.cpu().numpy(), ref_i)
+
+
+def test_topk_from_scores_ties(cuda):
+    from longcat_video.models.block_sparse_attention import topk_block_indices
+
+    g = np.random.default_rng(9)
+    s = g.integers(-2, 3, size=(1, 3, 50, 300)).astype(np.float32)
+    s[..., ::11] = -0.0
+    st = torch.from_numpy(s).to(cuda)
+    for k in (1, 17, 150, 300):
+        got, n = topk_block_indices(st, sparsity=0.0, topk=k)
+        ref, _ = orc.topk_block_indices(s, topk=k)
+        assert n == k and np.array_equal(got.cpu().numpy(), ref), k
+
+
+def test_block_scores_rectangular(cuda):
+    from longcat_video.models.block_sparse_attention import block_routing_scores
+
+    q = _rand((1, 2, 7, 32), torch.float32, 6, cuda)
+    k = _rand((1, 2, 13, 32), torch.float32, 7, cuda)
+    got = block_routing_scores(q, k)
+    ref = orc.block_routing_scores(_np(q), _np(k))
+    assert _np(got).tobytes() == ref.tobytes()
+
+
+def _random_indices(B, H, nb, k, seed):
+    g = np.random.default_rng(seed)
+    idx = np.stack([np.sort(g.choice(nb, size=k, replace=False)) for _ in range(B * H * nb)])
+    return idx.reshape(B, H, nb, k).astype(np.int32)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [128, 64, 16])
+@pytest.mark.parametrize("k", [1, 2, 5, 8])
+def test_attention_indices_vs_oracle(cuda, dtype, D, k):
+    from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
+
+    shape, chunk = (4, 8, 8), (4, 4, 4)  # 4 blocks... use a larger grid for k up to 8
+    shape = (8, 8, 8)
+    B, H, S = 1, 2, 512
+    nb = S // 64
+    q = _rand((B, H, S, D), dtype, 10 + D, cuda)
+    kk = _rand((B, H, S, D), dtype, 20 + D, cuda)
+    v = _rand((B, H, S, D), dtype, 30 + D, cuda)
+    idx = _random_indices(B, H, nb, k, 40 + k)
+    out = bsa_attention_cuda(q, kk, v, torch.from_numpy(idx).to(cuda), chunk_thw=chunk, shape=shape)
+    torch.cuda.synchronize()
+    ref = orc.bsa_sparse_attention(_np(q), _np(kk), _np(v), idx, shape, chunk)
+    _close(_np(out), ref)
+
+
+@pytest.mark.parametrize("geom", GEOMS)
+def test_attention_geometries(cuda, geom):
+    from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
+
+    shape, chunk = geom
+    if chunk[0] * chunk[1] * chunk[2] != 64:
+        pytest.skip("kernel uses 64-token blocks")
+    S = shape[0] * shape[1] * shape[2]
+    nb = S // 64
+    k = max(1, nb // 3)
+    q, kk, v = (_rand((1, 2, S, 128), torch.bfloat16, s, cuda) for s in (50, 51, 52))
+    idx = _random_indices(1, 2, nb, k, 53)
+    out = bsa_attention_cuda(q, kk, v, torch.from_numpy(idx).to(cuda), chunk_thw=chunk, shape=shape)
+    ref = orc.bsa_sparse_attention(_np(q), _np(kk), _np(v), idx, shape, chunk)
+    _close(_np(out), ref)
+
+
+def test_attention_single_block_equals_dense(cuda):
+    # reference tests/smoke/test_bsa_tier_b_smoke.py:47-79: one block, top-1 == dense SDPA
+    from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
+
+    q, k, v = (_rand((1, 2, 64, 128), torch.bfloat16, s, cuda) for s in (60, 61, 62))
+    out = bsa_attention_cuda(q, k, v, torch.zeros((1, 2, 1, 1), dtype=torch.int32, device=cuda),
+                             chunk_thw=(4, 4, 4), shape=(4, 4, 4))
+    dense = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float())
+    _close(_np(out), _np(dense))
+
+
+def test_attention_all_blocks_equals_dense(cuda):
+    # reference tests/smoke/test_bsa_tier_b_smoke.py:82-117: every q block attends to every block
+    from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
+
+    S = 1024
+    nb = S // 64
+    q, k, v = (_rand((1, 2, S, 128), torch.bfloat16, s, cuda) for s in (63, 64, 65))
+    idx = torch.arange(nb, dtype=torch.int32, device=cuda).expand(1, 2, nb, nb).contiguous()
+    out = bsa_attention_cuda(q, k, v, idx, chunk_thw=(1, 1, 64), shape=(1, 1, S))
+    dense = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float())
+    _close(_np(out), _np(dense))
+
+
+def test_attention_strided_inputs_match_contiguous(cuda):
+    from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
+
+    B, N, H, D = 1, 512, 4, 128
+    qkv = _rand((B, N, 3, H, D), torch.bfloat16, 70, cuda).permute(2, 0, 3, 1, 4)
+    q, k, v = qkv[0], qkv[1], qkv[2]
+    idx = torch.from_numpy(_random_indices(B, H, N // 64, 3, 71)).to(cuda)
+    a = bsa_attention_cuda(q, k, v, idx, chunk_thw=(4, 4, 4), shape=(8, 8, 8))
+    b = bsa_attention_cuda(q.contiguous(), k.contiguous(), v.contiguous(), idx, chunk_thw=(4, 4, 4), shape=(8, 8, 8))
+    assert torch.equal(a, b)
+
+
+def test_bad_block_index_sets_device_error(cuda):
+    from longcat_video import _native
+    from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
+
+    _native.device_error(clear=True)
+    q = _rand((1, 1, 128, 128), torch.bfloat16, 72, cuda)
+    idx = torch.tensor([[[[0, 1]], [[1, 1 << 20]]]], dtype=torch.int32, device=cuda).view(1, 1, 2, 2)
+    bsa_attention_cuda(q, q, q, idx, chunk_thw=(1, 1, 64), shape=(1, 1, 128))
+    assert _native.device_error(clear=True) == _native.BSA_ERR_INDEX
+
+
+def test_rejections(cuda):
+    from longcat_video.models.block_sparse_attention import bsa_attention
+    from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
+
+    q = _rand((1, 1, 96, 128), torch.bfloat16, 73, cuda)
+    with pytest.raises(ValueError, match="multiple of"):
+        bsa_attention(q, q, q, shape=(4, 4, 6), sparsity=0.9)
+    with pytest.raises(ValueError, match="required"):
+        bsa_attention_cuda(q, q, q, torch.zeros((1, 1, 1, 1), dtype=torch.int32, device=cuda))
+    with pytest.raises(ValueError, match="multiple of block_size"):
+        bsa_attention_cuda(q, q, q, torch.zeros((1, 1, 1, 1), dtype=torch.int32, device=cuda), shape=(1, 1, 96),
+                           chunk_thw=(1, 1, 64))
+    x = _rand((1, 1, 64, 128), torch.float32, 74, cuda)
+    with pytest.raises(ValueError, match="fp16 and bf16"):
+        bsa_attention_cuda(x, x, x, torch.zeros((1, 1, 1, 1), dtype=torch.int32, device=cuda), shape=(4, 4, 4))
+    y = _rand((1, 1, 64, 12), torch.bfloat16, 75, cuda)
+    with pytest.raises(ValueError, match="multiple of 8"):
+        bsa_attention_cuda(y, y, y, torch.zeros((1, 1, 1, 1), dtype=torch.int32, device=cuda), shape=(4, 4, 4))
+
+
+def _full_forward_check(q, k, v, shape, chunk, topk, heads=None, qblocks=None, rope=None):
+    """Engine forward vs oracle: indices exact on the checked heads, outputs within tolerance."""
+    from longcat_video.models.block_sparse_attention import bsa_attention
+
+    out, idx = bsa_attention(q, k, v, shape, chunk_thw=chunk, topk=topk, return_indices=True, rope=rope)
+    torch.cuda.synchronize()
+    hs = list(range(q.shape[1])) if heads is None else heads
+    qn, kn, vn = (_np(t[:, hs]) for t in (q, k, v))
+    if rope is not None:
+        cos, sin = orc.rope_full_tables(rope.grid, q.shape[-1])
+        dt = "bf16" if q.dtype == torch.bfloat16 else "fp16"
+        qn = orc.apply_rope(qn, cos, sin, dt)
+        kn = orc.apply_rope(kn, cos, sin, dt)
+    qb = orc.mean_pool_blocks_3d(qn, shape, chunk)
+    kb = orc.mean_pool_blocks_3d(kn, shape, chunk)
+    ref_idx, _ = orc.topk_block_indices(orc.block_routing_scores(qb, kb), topk=topk)
+    got_idx = idx[:, hs].cpu().numpy()
+    assert np.array_equal(got_idx, ref_idx)
+    ref = orc.bsa_sparse_attention(qn, kn, vn, ref_idx, shape, chunk, qblocks=qblocks)
+    got = _np(out[:, hs])
+    if qblocks is not None:
+        got = orc.to_block_major(got, shape, chunk)[:, :, qblocks].reshape(ref.shape)
+    return _close(got, ref)
+
+
+def test_forward_config1_bf16(cuda):
+    """Config 1 (H=4, S=4096, top-4) with the fp32 inputs rounded to bf16 on the device."""
+    from longcat_video.workloads import make_config1_numpy
+
+    q, k, v = (torch.from_numpy(a).to(cuda).to(torch.bfloat16) for a in make_config1_numpy(0))
+    _full_forward_check(q, k, v, (1, 1, 4096), (1, 1, 64), 4)
+
+
+def test_forward_config1_golden_indices(cuda):
+    """Config 1 fp32 routing on the engine equals the committed golden routing (oracle output)."""
+    import os
+
+    from longcat_video.models.block_sparse_attention import (block_routing_scores, mean_pool_blocks_3d,
+                                                             topk_block_indices)
+    from longcat_video.workloads import make_config1_numpy
+
+    gold = np.load(os.path.join(os.path.dirname(__file__), "golden", "config1.npz"))
+    q, k, _ = (torch.from_numpy(a).to(cuda) for a in make_config1_numpy(0))
+    qb = mean_pool_blocks_3d(q, (1, 1, 4096), (1, 1, 64))
+    kb = mean_pool_blocks_3d(k, (1, 1, 4096), (1, 1, 64))
+    idx, n = topk_block_indices(block_routing_scores(qb, kb), sparsity=0.9375)
+    assert n == 4
+    assert np.array_equal(idx.cpu().numpy(), gold["block_indices"])
+
+
+def test_forward_voxel_blocks_fp16(cuda):
+    q, k, v = (_rand((1, 4, 8 * 16 * 16, 128), torch.float16, s, cuda) for s in (80, 81, 82))
+    _full_forward_check(q, k, v, (8, 16, 16), (4, 4, 4), 5)
+
+
+def test_forward_fused_rope(cuda):
+    from longcat_video.models.rope_3d import RopeTables
+
+    grid = (4, 8, 16)
+    S = 512
+    q, k, v = (_rand((1, 2, S, 128), torch.bfloat16, s, cuda) for s in (83, 84, 85))
+    _full_forward_check(q, k, v, (1, 1, S), (1, 1, 64), 3, rope=RopeTables(grid, 128, cuda))
+
+
+def test_forward_config2_fullsize(cuda):
+    """Config 2 at full size: routing exact on two heads, outputs checked on sampled q blocks."""
+    from longcat_video.workloads import CONFIGS, make_qkv
+
+    cfg = CONFIGS["config2"]
+    q, k, v = make_qkv(cfg, cuda, seed=0)
+    _full_forward_check(q, k, v, cfg.shape, cfg.chunk, cfg.topk, heads=[0, 31], qblocks=[0, 1, 677, 1348, 1349])
+
+
+def test_forward_config3_fp16_near_ties(cuda):
+    """Config 3 (fp16, i.i.d. inputs, near-tied pooled scores): exact routing on 3 heads."""
+    from longcat_video.workloads import CONFIGS, make_qkv
+
+    cfg = CONFIGS["config3_s0.9375"]
+    q, k, v = make_qkv(cfg, cuda, seed=1, heads=3)
+    _full_forward_check(q, k, v, cfg.shape, cfg.chunk, cfg.topk, qblocks=[0, 5, 900])
+
+
+def test_attention_hook_routes_to_engine(cuda):
+    from longcat_video.models.attention import Attention
+
+    torch.manual_seed(0)
+    attn = Attention(256, 2).to(cuda).to(torch.bfloat16)
+    x = torch.randn((1, 512, 256), device=cuda, dtype=torch.bfloat16)
+    dense = attn(x, (8, 8, 8))
+    attn.enable_bsa = True
+    attn.bsa_sparsity = 0.0  # keep every block: must equal dense attention
+    sparse = attn(x, (8, 8, 8))
+    _close(_np(sparse), _np(dense))
+    attn.bsa_sparsity = 0.75
+    part = attn(x, (8, 8, 8))
+    assert torch.isfinite(part).all()

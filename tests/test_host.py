@@ -1,0 +1,143 @@
+"""Host-side logic on CPU: DiT BSA wiring (reference tests/smoke/test_bsa_dit_wiring_smoke.py),
+argument validation of the Python layer, workload definitions, and the Ulysses re-sharding on
+gloo ranks (world size 2)."""
+
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+
+def _cfg(enable_bsa=False):
+    return {"hidden_size": 64, "depth": 2, "num_heads": 4,
+            "bsa_params": {"sparsity": 0.9375, "chunk_3d_shape_q": [4, 4, 4], "chunk_3d_shape_k": [4, 4, 4]},
+            "enable_bsa": enable_bsa}
+
+
+def test_default_bsa_off():
+    from longcat_video.models.longcat_video_dit import LongCatVideoTransformer3DModel
+
+    dit = LongCatVideoTransformer3DModel.from_config(_cfg(False))
+    assert all(b.attn.enable_bsa is False for b in dit.blocks)
+
+
+def test_config_enable_bsa_flips_attention():
+    from longcat_video.models.longcat_video_dit import LongCatVideoTransformer3DModel
+
+    dit = LongCatVideoTransformer3DModel.from_config(_cfg(True))
+    for b in dit.blocks:
+        assert b.attn.enable_bsa is True
+        assert b.attn.bsa_sparsity == 0.9375
+        assert b.attn.bsa_chunk_thw == (4, 4, 4)
+
+
+def test_enable_disable_roundtrip_and_backends():
+    from longcat_video.models.longcat_video_dit import LongCatVideoTransformer3DModel
+
+    dit = LongCatVideoTransformer3DModel.from_config(_cfg(False))
+    for backend in ("tier_a", "metal", "metal_v2", "metal_v3", "metal_v4", "cuda"):
+        dit.enable_bsa(backend=backend)
+        assert all(b.attn.enable_bsa and b.attn.bsa_backend == backend for b in dit.blocks)
+    dit.disable_bsa()
+    assert all(b.attn.enable_bsa is False for b in dit.blocks)
+    with pytest.raises(AssertionError):
+        dit.enable_bsa(backend="triton")
+
+
+def test_bsa_params_preserved_through_enable():
+    from longcat_video.models.longcat_video_dit import LongCatVideoTransformer3DModel
+
+    cfg = _cfg(False)
+    cfg["bsa_params"]["sparsity"] = 0.5
+    cfg["bsa_params"]["chunk_3d_shape_q"] = [2, 2, 2]
+    dit = LongCatVideoTransformer3DModel.from_config(cfg)
+    dit.enable_bsa()
+    assert all(b.attn.bsa_sparsity == 0.5 and b.attn.bsa_chunk_thw == (2, 2, 2) for b in dit.blocks)
+
+
+def test_cpu_tensors_are_rejected_not_computed():
+    from longcat_video.models.block_sparse_attention import bsa_attention
+
+    q = torch.zeros((1, 1, 64, 128), dtype=torch.bfloat16)
+    with pytest.raises((ValueError, RuntimeError)):
+        bsa_attention(q, q, q, shape=(4, 4, 4))
+
+
+def test_python_geometry_errors_match_reference_wording():
+    from longcat_video import _native
+
+    with pytest.raises(ValueError, match="multiple of"):
+        _native._geometry(96, (4, 4, 6), (4, 4, 4))
+    with pytest.raises(ValueError, match="doesn't match"):
+        _native._geometry(100, (4, 4, 4), (4, 4, 4))
+
+
+def test_workload_configs():
+    from longcat_video.workloads import CONFIGS, ceil_topk
+
+    c2 = CONFIGS["config2"]
+    assert (c2.S, c2.nb, c2.topk) == (86400, 1350, 85)
+    assert c2.sparse_flops() == pytest.approx(7.70e12, rel=1e-3)
+    assert CONFIGS["config5"].nb == 2700 and CONFIGS["config5"].topk == 169
+    assert [ceil_topk(1350, s) for s in (0.75, 0.875, 0.9375)] == [338, 169, 85]
+    assert [CONFIGS[f"config3_s{s}"].topk for s in ("0.75", "0.875", "0.9375")] == [338, 169, 85]
+
+
+def test_build_token_block_indices_and_mask():
+    from longcat_video.models.block_sparse_attention import build_token_block_indices, build_token_pair_mask
+
+    t = build_token_block_indices((8, 4, 4), (4, 4, 4))
+    assert (t[:64] == 0).all() and (t[64:] == 1).all()
+    m = build_token_pair_mask(torch.tensor([[[[3, 5], [0, 7]]]]), torch.arange(8), 8)
+    assert m[0, 0, 0, 3] and m[0, 0, 0, 5] and not m[0, 0, 0, 0]
+
+
+# ------------------------------------------------------------------ Ulysses on gloo ranks
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _ulysses_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from longcat_video.context_parallel import heads_to_seq, seq_to_heads
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        B, H, S, D = 1, 4, 16, 3
+        full = torch.arange(B * H * S * D, dtype=torch.float32).reshape(B, H, S, D)
+        Sl = S // world
+        shard = full[:, :, rank * Sl:(rank + 1) * Sl].clone()
+        # q, k, v stacked travel in one collective
+        stacked = torch.stack((shard, shard + 1, shard + 2))
+        heads = seq_to_heads(stacked)
+        Hl = H // world
+        ok1 = torch.equal(heads[0], full[:, rank * Hl:(rank + 1) * Hl])
+        ok2 = torch.equal(heads[2], full[:, rank * Hl:(rank + 1) * Hl] + 2)
+        back = heads_to_seq(heads[1] * 10)
+        ok3 = torch.equal(back, (shard + 1) * 10)
+        q.put((rank, bool(ok1 and ok2 and ok3)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ulysses_resharding_gloo_world2():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ulysses_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}
