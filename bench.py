@@ -351,12 +351,18 @@ def main(argv=None):
     ap.add_argument("--ref-qblocks", type=int, default=256,
                     help="q blocks of one head in each CPU sample (bounds the CPU run time)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="override the head count (small cases for profiling; not a bench line)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
     from longcat_video.workloads import CONFIGS
 
     cfg = CONFIGS[args.config]
+    if args.heads:
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, H=args.heads)
     if args.impl == "reference":
         return run_reference(args, cfg)
     return run_ours(args, cfg)

@@ -9,17 +9,26 @@
 // full-rate M=128 shape:
 //     S^T[128 kv x 64 q]  = Kpair[128 x D] . Q^T          (A = K, K-major; B = Q, K-major)
 //     O^T[128 d  x 64 q] += Vpair^T[D x 128] . P^T        (A = V^T, MN-major; B = P^T, MN-major)
-// Both accumulators live in TMEM.  The column-wise (per query) online softmax uses a lazy
-// running max: it is only raised when a score exceeds it by more than 2^8, so the common step
-// needs no cross-thread max; the row sums are kept per thread and reduced once per block.
+// Both accumulators live in TMEM; O^T is split into two accumulation chains (one per KV block)
+// so consecutive PV MMAs do not wait on each other.
 //
-// Roles (256 threads, one CTA per SM, persistent over (head, q-block) units in head-major
-// order so a head's K/V stays resident in L2):
-//   warp 0     : TMA producer (Q tiles, K/V block pairs into a 3-stage ring)
-//   warp 1     : MMA issuer (one thread)
-//   warps 4-7  : softmax / correction / epilogue warpgroup (thread t <-> TMEM lane t)
-// Every mbarrier wait is bounded (bsa_ptx.cuh); a timeout records an error code and the CTA
-// winds down.
+// Softmax: column-wise (per query) online softmax with a lazy running max.  Every thread keeps
+// the running max of its group's 32 query columns in registers and forms t = S*scale*log2(e) - m
+// with one FMA; the max is only raised (and O^T / the row sums rescaled) when some t exceeds
+// 2^8, which one predicate-OR barrier per step detects.  Row sums stay per thread and are
+// reduced once per query block.
+//
+// The kernel needs every (q-block, kv-block) pair's own 32 KB of K and V from L2, so the roles
+// are decoupled so that no load waits behind an unrelated one:
+//   warp 0      : Q tiles + K pairs (3-slot ring of 32 KB pairs, a slot is freed when its QK completes)
+//   warp 1      : QK^T MMA issuer (one thread)
+//   warp 2      : V blocks (5-slot ring of 16 KB blocks, a slot is freed when its PV completes)
+//   warp 3      : PV MMA issuer (one thread)
+//   warps 4-7   : softmax group 0 -- query columns 0..31   (thread t <-> TMEM lane t)
+//   warps 8-11  : softmax group 1 -- query columns 32..63
+// One CTA per SM, persistent over (head, q-block) units in head-major order so a head's K/V stays
+// resident in L2.  Every mbarrier wait is bounded (bsa_ptx.cuh); a timeout records an error code
+// and the CTA winds down.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -29,43 +38,58 @@
 namespace bsa {
 
 namespace attn {
-constexpr int kBlock = 64;            // tokens per block
-constexpr int kDP = 128;              // head dim as laid out in shared memory (zero padded)
-constexpr int kStages = 3;
-constexpr int kQBytes = kBlock * kDP * 2;          // 16 KB
-constexpr int kPairBytes = 2 * kBlock * kDP * 2;   // 32 KB (one operand of a block pair)
-constexpr int kStageBytes = 2 * kPairBytes;        // K pair + V pair = 64 KB
-constexpr int kTileBytes = 2 * kQBytes + kStages * kStageBytes;  // 224 KB
-constexpr int kThreads = 256;
-constexpr float kRescaleThreshold = 8.0f;          // log2 units: P <= 2^8 between rescales
+constexpr int kBlock = 64;                          // tokens per block
+constexpr int kDP = 128;                            // head dim in shared memory (zero padded)
+#ifndef BSA_KSTAGES
+#define BSA_KSTAGES 3
+#endif
+#ifndef BSA_VSLOTS
+#define BSA_VSLOTS 5
+#endif
+constexpr int kKStages = BSA_KSTAGES;               // K pairs
+constexpr int kVSlots = BSA_VSLOTS;                 // V single blocks
+constexpr int kQBytes = kBlock * kDP * 2;           // 16 KB
+constexpr int kPBytes = 2 * kBlock * 64 * 2;        // 16 KB: P^T [128 kv][64 q]
+constexpr int kPairBytes = 2 * kBlock * kDP * 2;    // 32 KB: K of a block pair
+constexpr int kVBlockBytes = kBlock * kDP * 2;      // 16 KB: V of one block
+constexpr int kOffQ = 0;
+constexpr int kOffP = kOffQ + 2 * kQBytes;
+constexpr int kOffK = kOffP + kPBytes;
+constexpr int kOffV = kOffK + kKStages * kPairBytes;
+constexpr int kTileBytes = kOffV + kVSlots * kVBlockBytes;
+constexpr int kThreads = 384;
+constexpr float kRescaleThreshold = 8.0f;           // log2 units: P <= 2^8 between rescales
 
-// TMEM column map (512 allocated): S^T double buffer, each split in two d-halves, and O^T
-// split in two kv-halves (independent accumulation chains hide the tensor-pipe latency).
-constexpr uint32_t kTmemCols = 512;
-__host__ __device__ constexpr uint32_t col_s(int buf, int half) { return buf * 128 + half * 64; }
-constexpr uint32_t kColO = 256;  // O^T.a at 256, O^T.b at 320
+// TMEM columns: S^T double buffer (64 columns each), O^T in two KV-block halves (64 columns each).
+// A softmax group owns 32 of the 64 columns of each.
+constexpr uint32_t kTmemCols = 256;
+__host__ __device__ constexpr uint32_t col_s(int buf) { return buf * 64; }
+constexpr uint32_t kColO = 128;
 
 struct SmallSmem {
-  uint64_t full[kStages];    // TMA -> MMA: stage loaded
-  uint64_t empty[kStages];   // MMA -> TMA: stage's PV done (stage free)
-  uint64_t s_full[2];        // MMA -> softmax: S^T ready
-  uint64_t s_empty[2];       // softmax -> MMA: S^T read
-  uint64_t p_full[2];        // softmax -> MMA: P^T written
-  uint64_t q_full[2];        // TMA -> MMA: Q tile loaded
-  uint64_t q_empty[2];       // MMA -> TMA: last QK of the unit done
-  uint64_t o_empty;          // softmax -> MMA: O^T read by the epilogue
-  uint64_t drain;            // teardown: all MMAs complete
+  uint64_t k_full[kKStages];
+  uint64_t k_empty[kKStages];
+  uint64_t v_full[kVSlots];
+  uint64_t v_empty[kVSlots];
+  uint64_t s_full[2];     // QK issuer -> softmax: S^T ready
+  uint64_t s_empty[2];    // softmax -> QK issuer: S^T read (256 arrivals)
+  uint64_t p_full;        // softmax -> PV issuer: P^T written (256 arrivals)
+  uint64_t p_empty;       // PV issuer -> softmax: PV done (P free, O^T up to date)
+  uint64_t q_full[2];
+  uint64_t q_empty[2];
+  uint64_t o_empty;       // softmax -> PV issuer: O^T read by the epilogue (256 arrivals)
+  uint64_t drain[2];
   uint32_t tmem_base;
   int abort_flag;
-  uint32_t flags[2][4][2];   // per-warp overflow bitmasks, double-buffered by step parity
-  alignas(16) float m[64];               // running max per query column (log2 domain)
-  alignas(16) float mthr[64];            // m + threshold
-  alignas(16) float alpha[64];           // rescale factors of the last max update; 1/l in the epilogue
-  alignas(16) float red[4][64];          // per-warp column partials (max or sum)
+  alignas(16) float red[4][64];  // per-warp column partials (max on the slow path, sums at the end)
+  alignas(16) float colv[64];    // per-column broadcast (max shift on the slow path, 1/l at the end)
+  alignas(16) float mcol[64];    // running max per query column (log2 domain)
 };
-constexpr int kSmemBytes = kTileBytes + 2048 + 1024;  // tiles + small + alignment slack
-static_assert(sizeof(SmallSmem) <= 2048, "small smem");
-static_assert(kSmemBytes <= 232448, "fits in 227 KB");
+// The whole 227 KB opt-in: tiles, small state, and what is left as slack to align the tiles to
+// 1024 bytes (checked at run time against the actual dynamic shared-memory base).
+constexpr int kSmemBytes = 232448;
+constexpr int kAlignSlack = kSmemBytes - kTileBytes - static_cast<int>(sizeof(SmallSmem));
+static_assert(kAlignSlack >= 0, "tiles and small state fit in 227 KB");
 
 struct Params {
   const int32_t* idx;   // [BH, nqb, topk]
@@ -74,11 +98,31 @@ struct Params {
   int Hl, Wl, cT, cH, cW, Bh, Bw;
   long long out_sb, out_sh, out_ss;
   float scale_log2;
-  int is_bf16;
   int total_units;
 };
 
 __device__ int g_attn_err;
+
+#ifdef BSA_PROFILE
+// Profiling builds only: per CTA and warp, cycles spent in up to 7 wait sites + the role's total.
+__device__ long long g_bsa_prof[1024][12][8];
+#define PACC(i) (&pacc[i])
+#define PTS_START() pts_last = clock64()
+#define PTS(i)                        \
+  do {                                \
+    const long long now_ = clock64(); \
+    pacc[i] += now_ - pts_last;       \
+    pts_last = now_;                  \
+  } while (0)
+#else
+#define PACC(i) nullptr
+#define PTS_START() \
+  do {              \
+  } while (0)
+#define PTS(i) \
+  do {         \
+  } while (0)
+#endif
 
 __device__ __forceinline__ void block_origin(const Params& p, int b, int& t0, int& h0, int& w0) {
   const int per_t = p.Bh * p.Bw;
@@ -109,68 +153,56 @@ __device__ __forceinline__ int named_bar_or(int id, int n, int pred) {
   return r;
 }
 
-// Transposed warp reduction: each lane holds v[0..63] (one value per query column) for its own
-// key row; afterwards lane L holds the reduction over the 32 lanes of columns
-// col(L, 0) and col(L, 1) where col(L, i) = 32*b4 + 16*b3 + 8*b2 + 4*b1 + 2*b0 + i (bK = bit K
-// of L).  62 shuffles instead of 64 x 5.
+// Transposed warp reduction over 32 columns: lane L holds v[0..31] (one value per column) for
+// its own key row; afterwards lane L holds the reduction over the 32 lanes of column L.
 template <bool kMax>
-__device__ __forceinline__ void transpose_reduce(float (&v)[64], float& r0, float& r1, int lane) {
+__device__ __forceinline__ float transpose_reduce32(float (&v)[32], int lane) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const bool up = lane & 16;
-    float send = up ? v[i] : v[i + 32];
-    float keep = up ? v[i + 32] : v[i];
-    float recv = __shfl_xor_sync(0xffffffffu, send, 16);
-    v[i] = kMax ? fmaxf(keep, recv) : keep + recv;
-  }
+  for (int lvl = 16; lvl >= 1; lvl >>= 1) {
+    const bool up = (lane & lvl) != 0;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const bool up = lane & 8;
-    float send = up ? v[i] : v[i + 16];
-    float keep = up ? v[i + 16] : v[i];
-    float recv = __shfl_xor_sync(0xffffffffu, send, 8);
-    v[i] = kMax ? fmaxf(keep, recv) : keep + recv;
+    for (int i = 0; i < lvl; ++i) {
+      const float send = up ? v[i] : v[i + lvl];
+      const float keep = up ? v[i + lvl] : v[i];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, lvl);
+      v[i] = kMax ? fmaxf(keep, recv) : keep + recv;
+    }
   }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const bool up = lane & 4;
-    float send = up ? v[i] : v[i + 8];
-    float keep = up ? v[i + 8] : v[i];
-    float recv = __shfl_xor_sync(0xffffffffu, send, 4);
-    v[i] = kMax ? fmaxf(keep, recv) : keep + recv;
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const bool up = lane & 2;
-    float send = up ? v[i] : v[i + 4];
-    float keep = up ? v[i + 4] : v[i];
-    float recv = __shfl_xor_sync(0xffffffffu, send, 2);
-    v[i] = kMax ? fmaxf(keep, recv) : keep + recv;
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const bool up = lane & 1;
-    float send = up ? v[i] : v[i + 2];
-    float keep = up ? v[i + 2] : v[i];
-    float recv = __shfl_xor_sync(0xffffffffu, send, 1);
-    v[i] = kMax ? fmaxf(keep, recv) : keep + recv;
-  }
-  r0 = v[0];
-  r1 = v[1];
+  return v[0];
 }
 
-__device__ __forceinline__ int transpose_col(int lane, int i) {
-  return ((lane >> 4) & 1) * 32 + ((lane >> 3) & 1) * 16 + ((lane >> 2) & 1) * 8 + ((lane >> 1) & 1) * 4 +
-         (lane & 1) * 2 + i;
+// Block ids of step j of a unit (the second id duplicates the first for an odd tail; those rows
+// are masked in the softmax).  Out-of-range ids are reported and replaced by block 0.
+__device__ __forceinline__ void step_blocks(const int32_t* idx, int j, int k, int nb, int* err, int& b0, int& b1) {
+  b0 = __ldg(idx + 2 * j);
+  b1 = (2 * j + 1 < k) ? __ldg(idx + 2 * j + 1) : b0;
+  if (static_cast<unsigned>(b0) >= static_cast<unsigned>(nb) || static_cast<unsigned>(b1) >= static_cast<unsigned>(nb)) {
+    atomicCAS(err, 0, BSA_ERR_INDEX);
+    b0 = static_cast<unsigned>(b0) >= static_cast<unsigned>(nb) ? 0 : b0;
+    b1 = static_cast<unsigned>(b1) >= static_cast<unsigned>(nb) ? 0 : b1;
+  }
 }
 
+template <bool kBF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  return kBF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+}
+
+template <bool kBF16>
 __global__ void __launch_bounds__(kThreads, 1)
     bsa_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                           // 2 x 16 KB
-  uint8_t* sStage = smem + 2 * kQBytes;         // 3 x 64 KB: [K pair 32 KB | V pair 32 KB]
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  if (pad > static_cast<uint32_t>(kAlignSlack)) {  // uniform across the CTA: nothing is set up yet
+    if (threadIdx.x == 0) atomicCAS(&g_attn_err, 0, 199);
+    return;
+  }
+  uint8_t* smem = smem_raw + pad;
+  uint8_t* sQ = smem + kOffQ;
+  uint8_t* sP = smem + kOffP;
+  uint8_t* sK = smem + kOffK;
+  uint8_t* sV = smem + kOffV;
   SmallSmem& ss = *reinterpret_cast<SmallSmem*>(smem + kTileBytes);
 
   const int tid = threadIdx.x;
@@ -178,19 +210,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = tid & 31;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&ss.full[s], 1);
-      mbar_init(&ss.empty[s], 1);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&ss.k_full[s], 1);
+      mbar_init(&ss.k_empty[s], 1);
+    }
+    for (int s = 0; s < kVSlots; ++s) {
+      mbar_init(&ss.v_full[s], 1);
+      mbar_init(&ss.v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ss.s_full[i], 1);
-      mbar_init(&ss.s_empty[i], 128);
-      mbar_init(&ss.p_full[i], 128);
+      mbar_init(&ss.s_empty[i], 256);
       mbar_init(&ss.q_full[i], 1);
       mbar_init(&ss.q_empty[i], 1);
+      mbar_init(&ss.drain[i], 1);
     }
-    mbar_init(&ss.o_empty, 128);
-    mbar_init(&ss.drain, 1);
+    mbar_init(&ss.p_full, 256);
+    mbar_init(&ss.p_empty, 1);
+    mbar_init(&ss.o_empty, 256);
     ss.abort_flag = 0;
     fence_mbar_init();
   }
@@ -201,6 +238,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ss.tmem_base;
+#ifdef BSA_PROFILE
+  const long long prof_t0 = clock64();
+  long long pacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  long long pts_last = 0;
+#endif
   volatile int* abort_flag = &ss.abort_flag;
   int* err = &g_attn_err;
 
@@ -209,23 +251,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int k = p.topk;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------------ Q + K producer
     if (lane == 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
-      prefetch_tmap(&tm_v);
-    }
-    long long g = 0;
-    int n = 0;
-    bool ok = true;
-    for (int unit = blockIdx.x; unit < p.total_units && ok; unit += G, ++n) {
-      const int bh = unit / p.nqb;
-      const int qblk = unit - bh * p.nqb;
-      const int32_t* idx = p.idx + (static_cast<long long>(bh) * p.nqb + qblk) * k;
-      if (lane == 0) {
+      long long g = 0;
+      int n = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.total_units && ok; unit += G, ++n) {
+        const int bh = unit / p.nqb;
+        const int qblk = unit - bh * p.nqb;
+        const int32_t* idx = p.idx + (static_cast<long long>(bh) * p.nqb + qblk) * k;
+        int nb0, nb1;
+        step_blocks(idx, 0, k, p.nqb, err, nb0, nb1);
         const int qb = n & 1;
-        if (n >= 2) ok = mbar_wait(&ss.q_empty[qb], ((n - 2) >> 1) & 1, abort_flag, err, 101);
-        if (ok) {
+        if (n >= 2) ok = mbar_wait(&ss.q_empty[qb], ((n - 2) >> 1) & 1, abort_flag, err, 101, PACC(0));
+        if (!ok) break;
+        {
           int t0, h0, w0;
           block_origin(p, qblk, t0, h0, w0);
           mbar_arrive_expect_tx(&ss.q_full[qb], kQBytes);
@@ -233,322 +275,355 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_5d(dst, &tm_q, &ss.q_full[qb], 0, w0, h0, t0, bh);
           tma_load_5d(dst + kQBytes / 2, &tm_q, &ss.q_full[qb], 64, w0, h0, t0, bh);
         }
-      }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      int nb0 = 0, nb1 = 0;
-      if (lane == 0) {
-        nb0 = __ldg(idx);
-        nb1 = (1 < k) ? __ldg(idx + 1) : nb0;
-      }
-      for (int j = 0; j < nsteps && ok; ++j, ++g) {
-        if (lane == 0) {
-          int b0 = nb0, b1 = nb1;
-          if (j + 1 < nsteps) {  // prefetch the next pair while this step waits for a free stage
-            nb0 = __ldg(idx + 2 * j + 2);
-            nb1 = (2 * j + 3 < k) ? __ldg(idx + 2 * j + 3) : nb0;
-          }
-          const int s = static_cast<int>(g % kStages);
-          if (g >= kStages) ok = mbar_wait(&ss.empty[s], static_cast<uint32_t>((g / kStages - 1) & 1), abort_flag, err, 102);
-          if (ok) {
-            if (static_cast<unsigned>(b0) >= static_cast<unsigned>(p.nqb) ||
-                static_cast<unsigned>(b1) >= static_cast<unsigned>(p.nqb)) {
-              atomicCAS(err, 0, BSA_ERR_INDEX);
-              b0 = static_cast<unsigned>(b0) >= static_cast<unsigned>(p.nqb) ? 0 : b0;
-              b1 = static_cast<unsigned>(b1) >= static_cast<unsigned>(p.nqb) ? 0 : b1;
-            }
-            uint8_t* st = sStage + s * kStageBytes;
-            mbar_arrive_expect_tx(&ss.full[s], kStageBytes);
+        for (int j = 0; j < nsteps && ok; ++j, ++g) {
+          const int b0 = nb0, b1 = nb1;
+          if (j + 1 < nsteps) step_blocks(idx, j + 1, k, p.nqb, err, nb0, nb1);  // prefetch next ids
+          const int ks = static_cast<int>(g % kKStages);
+          if (g >= kKStages)
+            ok = mbar_wait(&ss.k_empty[ks], static_cast<uint32_t>((g / kKStages - 1) & 1), abort_flag, err, 102,
+                           PACC(1));
+          if (!ok) break;
+          uint8_t* dst = sK + ks * kPairBytes;
+          mbar_arrive_expect_tx(&ss.k_full[ks], kPairBytes);
 #pragma unroll
-            for (int bi = 0; bi < 2; ++bi) {
-              int t0, h0, w0;
-              block_origin(p, bi ? b1 : b0, t0, h0, w0);
+          for (int bi = 0; bi < 2; ++bi) {
+            int t0, h0, w0;
+            block_origin(p, bi ? b1 : b0, t0, h0, w0);
 #pragma unroll
-              for (int hh = 0; hh < 2; ++hh) {
-                tma_load_5d(st + hh * 16384 + bi * 8192, &tm_k, &ss.full[s], hh * 64, w0, h0, t0, bh);
-                tma_load_5d(st + kPairBytes + hh * 16384 + bi * 8192, &tm_v, &ss.full[s], hh * 64, w0, h0, t0, bh);
-              }
-            }
+            for (int hh = 0; hh < 2; ++hh)
+              tma_load_5d(dst + hh * 16384 + bi * 8192, &tm_k, &ss.k_full[ks], hh * 64, w0, h0, t0, bh);
           }
         }
-        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       }
-    }
-    // teardown: make sure no TMA write into this CTA's shared memory is still in flight
-    if (lane == 0 && g > 0) {
-      const long long first = g > kStages ? g - kStages : 0;
-      for (long long gg = first; gg < g; ++gg) {
-        const int s = static_cast<int>(gg % kStages);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&ss.full[s], static_cast<uint32_t>((gg / kStages) & 1)) &&
+      // teardown: no TMA write into this CTA's shared memory may still be in flight
+      const uint64_t t0 = globaltimer_ns();
+      for (long long gg = (g > kKStages ? g - kKStages : 0); gg < g; ++gg)
+        while (!mbar_try_wait(&ss.k_full[gg % kKStages], static_cast<uint32_t>((gg / kKStages) & 1)) &&
                globaltimer_ns() - t0 < kWaitLimitNs) {
         }
-      }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    const uint32_t id_qk = idesc_f16(128, 64, p.is_bf16, 0, 0);
-    const uint32_t id_pv = idesc_f16(128, 64, p.is_bf16, 1, 1);
-    long long g = 0;
-    int n = 0;
-    bool ok = true;
-    bool have_prev = false;
-    long long prev_g = 0;
-    int prev_j = 0, prev_n = 0;
-    auto issue_pv = [&](long long gp, int jp, int np) -> bool {
-      const int s = static_cast<int>(gp % kStages);
-      const int pb = static_cast<int>(gp & 1);
-      if (!mbar_wait(&ss.p_full[pb], static_cast<uint32_t>((gp >> 1) & 1), abort_flag, err, 111)) return false;
-      if (jp == 0 && np >= 1) {
-        if (!mbar_wait(&ss.o_empty, static_cast<uint32_t>((np - 1) & 1), abort_flag, err, 112)) return false;
-      }
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t vb = smem_u32(sStage + s * kStageBytes + kPairBytes);
-        const uint32_t pbase = smem_u32(sStage + s * kStageBytes);
+    __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ V producer
+    if (lane == 0) {
+      prefetch_tmap(&tm_v);
+      long long gb = 0;  // V blocks issued
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.total_units && ok; unit += G) {
+        const int bh = unit / p.nqb;
+        const int qblk = unit - bh * p.nqb;
+        const int32_t* idx = p.idx + (static_cast<long long>(bh) * p.nqb + qblk) * k;
+        int nb0, nb1;
+        step_blocks(idx, 0, k, p.nqb, err, nb0, nb1);
+        for (int j = 0; j < nsteps && ok; ++j) {
+          const int b0 = nb0, b1 = nb1;
+          if (j + 1 < nsteps) step_blocks(idx, j + 1, k, p.nqb, err, nb0, nb1);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int kk = half * 4 + i;
-            const uint64_t ad = sdesc_sw128(vb + kk * 2048, 16384, 1024);
-            const uint64_t bd = sdesc_sw128(pbase + kk * 2048, 16384, 1024);
-            umma_ss(tmem + kColO + half * 64, ad, bd, id_pv, (jp > 0 || i > 0) ? 1u : 0u);
+          for (int bi = 0; bi < 2 && ok; ++bi, ++gb) {
+            const int vs = static_cast<int>(gb % kVSlots);
+            if (gb >= kVSlots)
+              ok = mbar_wait(&ss.v_empty[vs], static_cast<uint32_t>((gb / kVSlots - 1) & 1), abort_flag, err, 103,
+                             PACC(0));
+            if (!ok) break;
+            int t0, h0, w0;
+            block_origin(p, bi ? b1 : b0, t0, h0, w0);
+            uint8_t* dst = sV + vs * kVBlockBytes;
+            mbar_arrive_expect_tx(&ss.v_full[vs], kVBlockBytes);
+            tma_load_5d(dst, &tm_v, &ss.v_full[vs], 0, w0, h0, t0, bh);
+            tma_load_5d(dst + kVBlockBytes / 2, &tm_v, &ss.v_full[vs], 64, w0, h0, t0, bh);
           }
         }
-        umma_commit(&ss.empty[s]);
       }
-      __syncwarp();
-      return true;
-    };
-    for (int unit = blockIdx.x; unit < p.total_units && ok; unit += G, ++n) {
-      const int qb = n & 1;
-      for (int j = 0; j < nsteps && ok; ++j, ++g) {
-        const int s = static_cast<int>(g % kStages);
-        const int sb = static_cast<int>(g & 1);
-        ok = mbar_wait(&ss.full[s], static_cast<uint32_t>((g / kStages) & 1), abort_flag, err, 113);
-        if (ok && g >= 2) ok = mbar_wait(&ss.s_empty[sb], static_cast<uint32_t>(((g >> 1) - 1) & 1), abort_flag, err, 114);
-        if (ok && j == 0) ok = mbar_wait(&ss.q_full[qb], static_cast<uint32_t>((n >> 1) & 1), abort_flag, err, 115);
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t kb = smem_u32(sStage + s * kStageBytes);
+      const uint64_t t0 = globaltimer_ns();
+      for (long long gg = (gb > kVSlots ? gb - kVSlots : 0); gg < gb; ++gg)
+        while (!mbar_try_wait(&ss.v_full[gg % kVSlots], static_cast<uint32_t>((gg / kVSlots) & 1)) &&
+               globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ QK^T issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(128, 64, kBF16 ? 1 : 0, 0, 0);
+      long long g = 0;
+      int n = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.total_units && ok; unit += G, ++n) {
+        const int qb = n & 1;
+        for (int j = 0; j < nsteps && ok; ++j, ++g) {
+          const int ks = static_cast<int>(g % kKStages);
+          const int sb = static_cast<int>(g & 1);
+          ok = mbar_wait(&ss.k_full[ks], static_cast<uint32_t>((g / kKStages) & 1), abort_flag, err, 113, PACC(0));
+#ifdef BSA_MEMONLY
+          // measurement build: consume K/Q without math to time the load pipeline alone
+          if (ok && j == 0) ok = mbar_wait(&ss.q_full[qb], static_cast<uint32_t>((n >> 1) & 1), abort_flag, err, 115, PACC(2));
+          if (!ok) break;
+          mbar_arrive(&ss.k_empty[ks]);
+          if (j == nsteps - 1) mbar_arrive(&ss.q_empty[qb]);
+          (void)sb;
+          continue;
+#endif
+          if (ok && g >= 2)
+            ok = mbar_wait(&ss.s_empty[sb], static_cast<uint32_t>(((g >> 1) - 1) & 1), abort_flag, err, 114, PACC(1));
+          if (ok && j == 0) ok = mbar_wait(&ss.q_full[qb], static_cast<uint32_t>((n >> 1) & 1), abort_flag, err, 115, PACC(2));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t kb = smem_u32(sK + ks * kPairBytes);
           const uint32_t qbase = smem_u32(sQ + qb * kQBytes);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const int half = kk >> 2, i = kk & 3;
+            const uint64_t ad = sdesc_sw128(kb + half * 16384 + i * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(qbase + half * 8192 + i * 32, 16, 1024);
+            umma_ss(tmem + col_s(sb), ad, bd, idesc, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&ss.s_full[sb]);
+          umma_commit(&ss.k_empty[ks]);
+          if (j == nsteps - 1) umma_commit(&ss.q_empty[qb]);
+        }
+      }
+      umma_commit(&ss.drain[0]);  // teardown: this thread's MMAs complete before TMEM is released
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&ss.drain[0], 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+      }
+    }
+    __syncwarp();
+  } else if (warp == 3) {
+    // ------------------------------------------------------------------ PV issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(128, 64, kBF16 ? 1 : 0, 1, 1);
+      long long g = 0;
+      int n = 0;
+      bool ok = true;
+      const uint32_t pbase = smem_u32(sP);
+      for (int unit = blockIdx.x; unit < p.total_units && ok; unit += G, ++n) {
+        for (int j = 0; j < nsteps && ok; ++j, ++g) {
+          const long long gb0 = 2 * g;
+          const int vs0 = static_cast<int>(gb0 % kVSlots);
+          const int vs1 = static_cast<int>((gb0 + 1) % kVSlots);
+          ok = mbar_wait(&ss.v_full[vs0], static_cast<uint32_t>((gb0 / kVSlots) & 1), abort_flag, err, 116, PACC(0));
+          if (ok) ok = mbar_wait(&ss.v_full[vs1], static_cast<uint32_t>(((gb0 + 1) / kVSlots) & 1), abort_flag, err, 117, PACC(1));
+#ifdef BSA_MEMONLY
+          if (!ok) break;
+          mbar_arrive(&ss.v_empty[vs0]);
+          mbar_arrive(&ss.v_empty[vs1]);
+          continue;
+#endif
+          if (ok) ok = mbar_wait(&ss.p_full, static_cast<uint32_t>(g & 1), abort_flag, err, 111, PACC(2));
+          if (ok && j == 0 && n >= 1) ok = mbar_wait(&ss.o_empty, static_cast<uint32_t>((n - 1) & 1), abort_flag, err, 112, PACC(3));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t vb0 = smem_u32(sV + vs0 * kVBlockBytes);
+          const uint32_t vb1 = smem_u32(sV + vs1 * kVBlockBytes);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
-              const uint64_t ad = sdesc_sw128(kb + half * 16384 + i * 32, 16, 1024);
-              const uint64_t bd = sdesc_sw128(qbase + half * 8192 + i * 32, 16, 1024);
-              umma_ss(tmem + col_s(sb, half), ad, bd, id_qk, i > 0 ? 1u : 0u);
+              const int kk = half * 4 + i;
+              const uint64_t ad = sdesc_sw128((half ? vb1 : vb0) + i * 2048, kVBlockBytes / 2, 1024);
+              const uint64_t bd = sdesc_sw128(pbase + kk * 2048, 16384, 1024);
+              umma_ss(tmem + kColO + half * 64, ad, bd, idesc, (j > 0 || i > 0) ? 1u : 0u);
             }
           }
-          umma_commit(&ss.s_full[sb]);
-          if (j == nsteps - 1) umma_commit(&ss.q_empty[qb]);
+          umma_commit(&ss.v_empty[vs0]);
+          umma_commit(&ss.v_empty[vs1]);
+          umma_commit(&ss.p_empty);
         }
-        __syncwarp();
-        if (have_prev) ok = issue_pv(prev_g, prev_j, prev_n);
-        have_prev = true;
-        prev_g = g;
-        prev_j = j;
-        prev_n = n;
       }
-    }
-    if (ok && have_prev) ok = issue_pv(prev_g, prev_j, prev_n);
-    // teardown: wait until every issued MMA has completed before TMEM is released
-    if (lane == 0) {
-      umma_commit(&ss.drain);
+      umma_commit(&ss.drain[1]);
       const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait(&ss.drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+      while (!mbar_try_wait(&ss.drain[1], 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
       }
     }
     __syncwarp();
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------------ softmax warpgroup
-    const int t = tid - 128;               // TMEM lane == key row (S^T) == d row (O^T)
-    const int wq = warp - 4;               // warp quarter
-    const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
-    const float scale_log2 = p.scale_log2;
-    const bool odd_tail = (k & 1) != 0;
-    long long g = 0;
-    int n = 0;
-    bool ok = true;
-    for (int unit = blockIdx.x; unit < p.total_units && ok; unit += G, ++n) {
-      const int bh = unit / p.nqb;
-      const int qblk = unit - bh * p.nqb;
-      if (t < 64) {
-        ss.m[t] = -INFINITY;
-        ss.mthr[t] = -INFINITY;
-      }
-      float l_part[64];
+  } else {
+    // ------------------------------------------------------------------ softmax groups
+#ifdef BSA_MEMONLY
+    if (true) {
+    } else
+#endif
+    {
+      const int grp = (warp - 4) >> 2;        // 0: columns 0..31, 1: columns 32..63
+      const int wq = warp & 3;                // TMEM lane quarter
+      const int t = wq * 32 + lane;           // TMEM lane == key row (S^T) == d row (O^T)
+      const int c0 = grp * 32;                // first query column of this group
+      const int bar_id = 1 + grp;
+      const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
+      const float scale_log2 = p.scale_log2;
+      const bool odd_tail = (k & 1) != 0;
+      long long g = 0;
+      int n = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < p.total_units && ok; unit += G, ++n) {
+        const int bh = unit / p.nqb;
+        const int qblk = unit - bh * p.nqb;
+        // mcol[c0 + q]: running max of query column c0+q (log2 domain), shared by the group
+        float l_part[32];
 #pragma unroll
-      for (int q = 0; q < 64; ++q) l_part[q] = 0.f;
-      named_bar_sync(1, 128);
-      for (int j = 0; j < nsteps && ok; ++j, ++g) {
-        const int s = static_cast<int>(g % kStages);
-        const int sb = static_cast<int>(g & 1);
-        ok = mbar_wait(&ss.s_full[sb], static_cast<uint32_t>((g >> 1) & 1), abort_flag, err, 121);
-        if (!ok) break;
-        tc_fence_after();
-        float x[64];
-        {
-          uint32_t ra[32], rb[32];
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld32(tmem + lane_base + col_s(sb, 0) + c * 32, ra);
-            tmem_ld32(tmem + lane_base + col_s(sb, 1) + c * 32, rb);
+        for (int q = 0; q < 32; ++q) l_part[q] = 0.f;
+        if (t < 32) ss.mcol[c0 + t] = 0.f;
+        named_bar_sync(bar_id, 128);
+        const float4* mvec = reinterpret_cast<const float4*>(&ss.mcol[c0]);
+        for (int j = 0; j < nsteps && ok; ++j, ++g) {
+          const int sb = static_cast<int>(g & 1);
+          ok = mbar_wait(&ss.s_full[sb], static_cast<uint32_t>((g >> 1) & 1), abort_flag, err, 121, PACC(0));
+          if (!ok) break;
+          PTS_START();
+          tc_fence_after();
+          const bool masked = odd_tail && j == nsteps - 1 && t >= 64;
+          float x[32];  // x = S*scale*log2e - m
+          {
+            uint32_t r[32];
+            tmem_ld32(tmem + lane_base + col_s(sb) + c0, r);
             tmem_ld_wait();
 #pragma unroll
-            for (int q = 0; q < 32; ++q)
-              x[c * 32 + q] = (__uint_as_float(ra[q]) + __uint_as_float(rb[q])) * scale_log2;
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(&ss.s_empty[sb]);
-        if (odd_tail && j == nsteps - 1 && t >= 64) {
+            for (int q4 = 0; q4 < 8; ++q4) {
+              const float4 mv = mvec[q4];
+              const float mq[4] = {mv.x, mv.y, mv.z, mv.w};
 #pragma unroll
-          for (int q = 0; q < 64; ++q) x[q] = -INFINITY;
-        }
-        // ---- lazy running max: find columns where some key exceeds m + threshold
-        uint32_t bits0 = 0, bits1 = 0;
-#pragma unroll
-        for (int q = 0; q < 32; ++q) bits0 |= (x[q] > ss.mthr[q] ? 1u : 0u) << q;
-#pragma unroll
-        for (int q = 0; q < 32; ++q) bits1 |= (x[q + 32] > ss.mthr[q + 32] ? 1u : 0u) << q;
-        bits0 = __reduce_or_sync(0xffffffffu, bits0);
-        bits1 = __reduce_or_sync(0xffffffffu, bits1);
-        if (lane == 0) {
-          ss.flags[sb][wq][0] = bits0;
-          ss.flags[sb][wq][1] = bits1;
-        }
-        named_bar_sync(1, 128);
-        bits0 = ss.flags[sb][0][0] | ss.flags[sb][1][0] | ss.flags[sb][2][0] | ss.flags[sb][3][0];
-        bits1 = ss.flags[sb][0][1] | ss.flags[sb][1][1] | ss.flags[sb][2][1] | ss.flags[sb][3][1];
-        if ((bits0 | bits1) != 0u) {
-          // exact column max over the 128 keys of this step, then raise m where needed
-          float tmp[64];
-#pragma unroll
-          for (int q = 0; q < 64; ++q) tmp[q] = x[q];
-          float r0, r1;
-          transpose_reduce<true>(tmp, r0, r1, lane);
-          ss.red[wq][transpose_col(lane, 0)] = r0;
-          ss.red[wq][transpose_col(lane, 1)] = r1;
-          named_bar_sync(1, 128);
-          bool any_rescale = false;
-          if (t < 64) {
-            const float mo = ss.m[t];
-            const float cm = fmaxf(fmaxf(ss.red[0][t], ss.red[1][t]), fmaxf(ss.red[2][t], ss.red[3][t]));
-            float mn = mo, a = 1.f;
-            if (cm > ss.mthr[t]) {
-              mn = fmaxf(mo, cm);
-              a = (mo == -INFINITY) ? 0.f : ex2_approx(mo - mn);
-            }
-            ss.m[t] = mn;
-            ss.mthr[t] = mn + kRescaleThreshold;
-            ss.alpha[t] = a;
-            any_rescale = a != 1.f;
-          }
-          const int need = named_bar_or(1, 128, any_rescale ? 1 : 0);
-          if (need && j > 0) {
-            // O^T columns must be rescaled: wait for the previous step's PV, then load/scale/store
-            const long long gp = g - 1;
-            ok = mbar_wait(&ss.empty[gp % kStages], static_cast<uint32_t>((gp / kStages) & 1), abort_flag, err, 122);
-            if (!ok) break;
-            tc_fence_after();
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-#pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                uint32_t r[16];
-                const uint32_t a = tmem + lane_base + kColO + half * 64 + c * 16;
-                tmem_ld16(a, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int q = 0; q < 16; ++q) r[q] = __float_as_uint(__uint_as_float(r[q]) * ss.alpha[c * 16 + q]);
-                tmem_st16(a, r);
+              for (int e = 0; e < 4; ++e) {
+                const int q = 4 * q4 + e;
+                x[q] = masked ? -INFINITY : fmaf(__uint_as_float(r[q]), scale_log2, -mq[e]);
               }
             }
-            tmem_st_wait();
           }
-          if (need) {
+          PTS(4);
+          // ---- lazy running max: does any key of the group exceed m + threshold?
+          float mx = x[0];
 #pragma unroll
-            for (int q = 0; q < 64; ++q) l_part[q] *= ss.alpha[q];
+          for (int q = 1; q < 32; ++q) mx = fmaxf(mx, x[q]);
+          const int over = named_bar_or(bar_id, 128, (j == 0 || mx > kRescaleThreshold) ? 1 : 0);
+          if (over) {
+            // slow path (first step of a block, or a large jump of the max): exact column max,
+            // reduced in place, then x is reloaded from TMEM (S is released only after this)
+            ss.red[wq][c0 + lane] = transpose_reduce32<true>(x, lane);
+            {
+              uint32_t r[32];
+              tmem_ld32(tmem + lane_base + col_s(sb) + c0, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int q = 0; q < 32; ++q)
+                x[q] = masked ? -INFINITY : fmaf(__uint_as_float(r[q]), scale_log2, -ss.mcol[c0 + q]);
+            }
+            named_bar_sync(bar_id, 128);
+            if (t < 32) {
+              const int c = c0 + t;
+              const float cm = fmaxf(fmaxf(ss.red[0][c], ss.red[1][c]), fmaxf(ss.red[2][c], ss.red[3][c]));
+              // shift of column c: the new max on the first step, else only when it jumps by > 2^8
+              const float d = (j == 0 || cm > kRescaleThreshold) ? cm : 0.f;
+              ss.colv[c] = d;
+              ss.mcol[c] += d;
+            }
+            const int need = named_bar_or(bar_id, 128, (t < 32 && j > 0 && ss.colv[c0 + t] != 0.f) ? 1 : 0);
+#pragma unroll
+            for (int q = 0; q < 32; ++q) x[q] -= ss.colv[c0 + q];
+            if (need) {
+              // O^T columns of this group must be rescaled: the previous step's PV must be complete
+              ok = mbar_wait(&ss.p_empty, static_cast<uint32_t>((g - 1) & 1), abort_flag, err, 122, PACC(3));
+              if (!ok) break;
+              tc_fence_after();
+#pragma unroll
+              for (int half = 0; half < 2; ++half) {
+                uint32_t r[32];
+                const uint32_t a = tmem + lane_base + kColO + half * 64 + c0;
+                tmem_ld32(a, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int q = 0; q < 32; ++q)
+                  r[q] = __float_as_uint(__uint_as_float(r[q]) * ex2_approx(-ss.colv[c0 + q]));
+                tmem_st32(a, r);
+              }
+              tmem_st_wait();
+#pragma unroll
+              for (int q = 0; q < 32; ++q) l_part[q] *= ex2_approx(-ss.colv[c0 + q]);
+            }
+            named_bar_sync(bar_id, 128);  // colv is rewritten by the next slow path
           }
-        }
-        // ---- probabilities, row-sum partials, P^T row into the consumed K slot of this stage
-        uint32_t packed[32];
+          tc_fence_before();
+          mbar_arrive(&ss.s_empty[sb]);
+          PTS(5);
+          // ---- probabilities, row-sum partials, P^T row into the P buffer
+          uint32_t packed[16];
 #pragma unroll
-        for (int q = 0; q < 64; q += 2) {
-          const float p0 = ex2_approx(x[q] - ss.m[q]);
-          const float p1 = ex2_approx(x[q + 1] - ss.m[q + 1]);
-          l_part[q] += p0;
-          l_part[q + 1] += p1;
-          packed[q >> 1] = p.is_bf16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
-        }
-        uint8_t* prow = sStage + s * kStageBytes;
+          for (int q = 0; q < 32; q += 2) {
+            const float p0 = ex2_approx(x[q]);
+            const float p1 = ex2_approx(x[q + 1]);
+            l_part[q] += p0;
+            l_part[q + 1] += p1;
+            packed[q >> 1] = pack2<kBF16>(p0, p1);
+          }
+          PTS(6);
+          if (g >= 1) {  // the previous step's PV must be done reading the P buffer
+            ok = mbar_wait(&ss.p_empty, static_cast<uint32_t>((g - 1) & 1), abort_flag, err, 124, PACC(1));
+            if (!ok) break;
+          }
+          PTS_START();
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 v = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-          *reinterpret_cast<uint4*>(prow + sw128_offset(static_cast<uint32_t>(t), static_cast<uint32_t>(c))) = v;
+          for (int c = 0; c < 4; ++c) {
+            const uint4 v = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+            *reinterpret_cast<uint4*>(sP + sw128_offset(static_cast<uint32_t>(t), static_cast<uint32_t>(grp * 4 + c))) = v;
+          }
+          fence_proxy_async_smem();
+          tc_fence_before();
+          mbar_arrive(&ss.p_full);
+          PTS(3);
         }
-        fence_proxy_async_smem();
+        if (!ok) break;
+        // ---- epilogue: row sums, O^T / l -> out (this group's 32 query rows)
+        ss.red[wq][c0 + lane] = transpose_reduce32<false>(l_part, lane);
+        ok = mbar_wait(&ss.p_empty, static_cast<uint32_t>((g - 1) & 1), abort_flag, err, 123, PACC(2));
+        if (!ok) break;
+        tc_fence_after();
+        float o[32];
+        {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tmem + lane_base + kColO + c0, ra);
+          tmem_ld32(tmem + lane_base + kColO + 64 + c0, rb);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 32; ++q) o[q] = __uint_as_float(ra[q]) + __uint_as_float(rb[q]);
+        }
         tc_fence_before();
-        mbar_arrive(&ss.p_full[sb]);
-      }
-      if (!ok) break;
-      // ---- epilogue: row sums, O^T / l -> out
-      {
-        float r0, r1;
-        transpose_reduce<false>(l_part, r0, r1, lane);
-        ss.red[wq][transpose_col(lane, 0)] = r0;
-        ss.red[wq][transpose_col(lane, 1)] = r1;
-      }
-      const long long gl = g - 1;
-      ok = mbar_wait(&ss.empty[gl % kStages], static_cast<uint32_t>((gl / kStages) & 1), abort_flag, err, 123);
-      if (!ok) break;
-      tc_fence_after();
-      float o[64];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t ra[16], rb[16];
-        tmem_ld16(tmem + lane_base + kColO + c * 16, ra);
-        tmem_ld16(tmem + lane_base + kColO + 64 + c * 16, rb);
-        tmem_ld_wait();
-#pragma unroll
-        for (int q = 0; q < 16; ++q) o[c * 16 + q] = __uint_as_float(ra[q]) + __uint_as_float(rb[q]);
-      }
-      tc_fence_before();
-      mbar_arrive(&ss.o_empty);
-      named_bar_sync(1, 128);
-      if (t < 64) {
-        const float l = ss.red[0][t] + ss.red[1][t] + ss.red[2][t] + ss.red[3][t];
-        ss.alpha[t] = l > 0.f ? 1.f / l : 0.f;
-      }
-      named_bar_sync(1, 128);
-      if (t < p.D) {
-        int t0, h0, w0;
-        block_origin(p, qblk, t0, h0, w0);
-        const int b = bh / p.H;
-        const int h = bh - b * p.H;
-        const long long base = b * p.out_sb + h * p.out_sh + t;
-        const int cHW = p.cH * p.cW;
-#pragma unroll
-        for (int q = 0; q < 64; ++q) {
-          const int ct = q / cHW;
-          const int rem = q - ct * cHW;
-          const int ch = rem / p.cW;
-          const int cw = rem - ch * p.cW;
-          const long long tok = (static_cast<long long>(t0 + ct) * p.Hl + (h0 + ch)) * p.Wl + (w0 + cw);
-          const float val = o[q] * ss.alpha[q];
-          if (p.is_bf16)
-            reinterpret_cast<__nv_bfloat16*>(p.out)[base + tok * p.out_ss] = __float2bfloat16_rn(val);
-          else
-            reinterpret_cast<__half*>(p.out)[base + tok * p.out_ss] = __float2half_rn(val);
+        mbar_arrive(&ss.o_empty);
+        named_bar_sync(bar_id, 128);
+        if (t < 32) {
+          const int c = c0 + t;
+          const float l = ss.red[0][c] + ss.red[1][c] + ss.red[2][c] + ss.red[3][c];
+          ss.colv[c] = l > 0.f ? 1.f / l : 0.f;
         }
+        named_bar_sync(bar_id, 128);
+        if (t < p.D) {
+          int t0, h0, w0;
+          block_origin(p, qblk, t0, h0, w0);
+          const int b = bh / p.H;
+          const int h = bh - b * p.H;
+          const long long base = b * p.out_sb + h * p.out_sh + t;
+          const int cHW = p.cH * p.cW;
+#pragma unroll
+          for (int q = 0; q < 32; ++q) {
+            const int r = c0 + q;
+            const int ct = r / cHW;
+            const int rem = r - ct * cHW;
+            const int ch = rem / p.cW;
+            const int cw = rem - ch * p.cW;
+            const long long tok = (static_cast<long long>(t0 + ct) * p.Hl + (h0 + ch)) * p.Wl + (w0 + cw);
+            const float val = o[q] * ss.colv[r];
+            if (kBF16)
+              reinterpret_cast<__nv_bfloat16*>(p.out)[base + tok * p.out_ss] = __float2bfloat16_rn(val);
+            else
+              reinterpret_cast<__half*>(p.out)[base + tok * p.out_ss] = __float2half_rn(val);
+          }
+        }
+        named_bar_sync(bar_id, 128);
       }
-      named_bar_sync(1, 128);
     }
   }
   // ------------------------------------------------------------------ teardown
+#ifdef BSA_PROFILE
+  pacc[7] = clock64() - prof_t0;
+  if (lane == 0 && blockIdx.x < 1024)
+    for (int i = 0; i < 8; ++i) g_bsa_prof[blockIdx.x][warp][i] = pacc[i];
+#endif
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -565,8 +640,10 @@ int launch_attn(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensor
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(bsa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(bsa_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(bsa_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess)
       return BSA_ERR_CUDA;
     configured[dev] = true;
   }
@@ -592,13 +669,24 @@ int launch_attn(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensor
   p.out_sh = a.out_sh;
   p.out_ss = a.out_ss;
   p.scale_log2 = a.sm_scale * 1.4426950408889634f;
-  p.is_bf16 = a.is_bf16;
   p.total_units = p.BH * a.nb;
   const int grid = p.total_units < sms ? p.total_units : sms;
   if (grid <= 0) return BSA_OK;
-  bsa_attn_kernel<<<grid, kThreads, kSmemBytes, stream>>>(*tm_q, *tm_k, *tm_v, p);
+  if (a.is_bf16)
+    bsa_attn_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(*tm_q, *tm_k, *tm_v, p);
+  else
+    bsa_attn_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(*tm_q, *tm_k, *tm_v, p);
   return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
 }
+
+#ifdef BSA_PROFILE
+extern "C" int bsa_prof_read(long long* out, int clear) {
+  (void)clear;
+  if (cudaDeviceSynchronize() != cudaSuccess) return BSA_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(out, attn::g_bsa_prof, sizeof(attn::g_bsa_prof)) != cudaSuccess) return BSA_ERR_CUDA;
+  return BSA_OK;
+}
+#endif
 
 int attn_device_error(int clear) {
   int v = 0;

@@ -154,7 +154,10 @@ int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t 
 int bsa_score_topk(const float* q_pooled, const float* k_pooled, int BH, int nb, int D, int topk,
                    int32_t* block_indices, float* scores, void* stream) {
   if (!q_pooled || !k_pooled || !block_indices) return fail(BSA_ERR_ARG, "null pointer");
-  if (BH <= 0 || nb <= 0 || D <= 0 || D > 128) return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nb=%d D=%d", BH, nb, D);
+  if (BH <= 0 || nb <= 0 || D <= 0 || D > 128 || D % 4)
+    return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nb=%d D=%d (D must be a multiple of 4, at most 128)", BH, nb, D);
+  if ((reinterpret_cast<uintptr_t>(q_pooled) | reinterpret_cast<uintptr_t>(k_pooled)) & 15u)
+    return fail(BSA_ERR_ALIGN, "pooled blocks must be 16-byte aligned");
   if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
   bsa::ScoreArgs a;
   a.qp = q_pooled; a.kp = k_pooled; a.BH = BH; a.nq = nb; a.nk = nb; a.D = D; a.topk = topk;
@@ -168,8 +171,11 @@ int bsa_score_topk(const float* q_pooled, const float* k_pooled, int BH, int nb,
 int bsa_block_scores(const float* q_pooled, const float* k_pooled, int BH, int nq, int nk, int D, float* scores,
                      void* stream) {
   if (!q_pooled || !k_pooled || !scores) return fail(BSA_ERR_ARG, "null pointer");
-  if (BH <= 0 || nq <= 0 || nk <= 0 || D <= 0 || D > 128)
-    return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nq=%d nk=%d D=%d", BH, nq, nk, D);
+  if (BH <= 0 || nq <= 0 || nk <= 0 || D <= 0 || D > 128 || D % 4)
+    return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nq=%d nk=%d D=%d (D must be a multiple of 4, at most 128)", BH, nq,
+                nk, D);
+  if ((reinterpret_cast<uintptr_t>(q_pooled) | reinterpret_cast<uintptr_t>(k_pooled)) & 15u)
+    return fail(BSA_ERR_ALIGN, "pooled blocks must be 16-byte aligned");
   bsa::ScoreArgs a;
   a.qp = q_pooled; a.kp = k_pooled; a.BH = BH; a.nq = nq; a.nk = nk; a.D = D; a.topk = 1;
   a.idx = nullptr; a.scores = scores; a.scores_in = nullptr;

@@ -287,10 +287,19 @@ __global__ void __launch_bounds__(kThreads) score_topk_kernel(Args a) {
       srow[static_cast<size_t>(i) * a.nk + j] = a.sin[(static_cast<long long>(bh) * a.nq + q0 + i) * a.nk + j];
     }
   } else {
-    // ---- stage the q tile transposed: qT[d][i]
-    for (int e = tid; e < a.QT * a.D; e += kThreads) {
-      const int i = e / a.D, d = e - i * a.D;
-      qT[d * a.QT + i] = (i < qn) ? qp[static_cast<long long>(i) * a.D + d] : 0.f;
+    // ---- stage the q tile transposed: qT[d][i ^ qswz(d)] (coalesced float4 reads; the XOR
+    //      keeps groups of 4 queries contiguous and spreads the transposed stores over banks)
+    const int D4 = a.D >> 2;
+    const int qmask = (a.QT >> 2) - 1;
+    for (int e = tid; e < a.QT * D4; e += kThreads) {
+      const int i = e / D4, d4 = e - i * D4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < qn) v = __ldg(reinterpret_cast<const float4*>(qp + static_cast<long long>(i) * a.D) + d4);
+      const int col = i ^ ((d4 & qmask) << 2);
+      qT[(4 * d4 + 0) * a.QT + col] = v.x;
+      qT[(4 * d4 + 1) * a.QT + col] = v.y;
+      qT[(4 * d4 + 2) * a.QT + col] = v.z;
+      qT[(4 * d4 + 3) * a.QT + col] = v.w;
     }
     // thread tile: 4 query rows x 2 key blocks
     const int ngroups = a.QT / 4;
@@ -300,21 +309,27 @@ __global__ void __launch_bounds__(kThreads) score_topk_kernel(Args a) {
     for (int j0 = 0; j0 < a.nk; j0 += kJT) {
       const int jn = min(kJT, a.nk - j0);
       __syncthreads();
-      for (int e = tid; e < kJT * a.D; e += kThreads) {
-        const int j = e / a.D, d = e - j * a.D;
-        kT[d * kJT + j] = (j < jn) ? kp[static_cast<long long>(j0 + j) * a.D + d] : 0.f;
+      // kT[d][j ^ kswz(d)], kswz even so key pairs (2p, 2p+1) stay contiguous
+      for (int e = tid; e < kJT * D4; e += kThreads) {
+        const int j = e / D4, d4 = e - j * D4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < jn) v = __ldg(reinterpret_cast<const float4*>(kp + static_cast<long long>(j0 + j) * a.D) + d4);
+        const int col = j ^ ((d4 & 15) << 1);
+        kT[(4 * d4 + 0) * kJT + col] = v.x;
+        kT[(4 * d4 + 1) * kJT + col] = v.y;
+        kT[(4 * d4 + 2) * kJT + col] = v.z;
+        kT[(4 * d4 + 3) * kJT + col] = v.w;
       }
       __syncthreads();
       if (active) {
         float acc[4][2];
   #pragma unroll
         for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = 0.f;
-        const float* qcol = qT + qg * 4;
-        const float* kcol = kT + jp * 2;
   #pragma unroll 8
         for (int d = 0; d < a.D; ++d) {
-          const float4 qv = *reinterpret_cast<const float4*>(qcol + d * a.QT);
-          const float2 kv = *reinterpret_cast<const float2*>(kcol + d * kJT);
+          const int d4 = d >> 2;
+          const float4 qv = *reinterpret_cast<const float4*>(qT + d * a.QT + ((qg * 4) ^ ((d4 & qmask) << 2)));
+          const float2 kv = *reinterpret_cast<const float2*>(kT + d * kJT + ((jp * 2) ^ ((d4 & 15) << 1)));
           acc[0][0] = __fmaf_rn(qv.x, kv.x, acc[0][0]);
           acc[0][1] = __fmaf_rn(qv.x, kv.y, acc[0][1]);
           acc[1][0] = __fmaf_rn(qv.y, kv.x, acc[1][0]);
