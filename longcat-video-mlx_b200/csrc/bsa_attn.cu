@@ -12,11 +12,11 @@
 // Both accumulators live in TMEM; O^T is split into two accumulation chains (one per KV block)
 // so consecutive PV MMAs do not wait on each other.
 //
-// Softmax: column-wise (per query) online softmax with a lazy running max.  Every thread keeps
-// the running max of its group's 32 query columns in registers and forms t = S*scale*log2(e) - m
-// with one FMA; the max is only raised (and O^T / the row sums rescaled) when some t exceeds
-// 2^8, which one predicate-OR barrier per step detects.  Row sums stay per thread and are
-// reduced once per query block.
+// Softmax: column-wise (per query) online softmax with a lazy running max.  A softmax group (4
+// warps, one per TMEM lane quarter) owns 16 query columns; every thread forms
+// x = S*scale*log2(e) - m with one FMA against the group's running maxima; the max is only raised
+// (and O^T / the row sums rescaled) when some x exceeds 2^8, which one predicate-OR barrier per
+// step detects.  Row sums stay per thread and are reduced once per query block.
 //
 // The kernel needs every (q-block, kv-block) pair's own 32 KB of K and V from L2, so the roles
 // are decoupled so that no load waits behind an unrelated one:
@@ -24,8 +24,7 @@
 //   warp 1      : QK^T MMA issuer (one thread)
 //   warp 2      : V blocks (5-slot ring of 16 KB blocks, a slot is freed when its PV completes)
 //   warp 3      : PV MMA issuer (one thread)
-//   warps 4-7   : softmax group 0 -- query columns 0..31   (thread t <-> TMEM lane t)
-//   warps 8-11  : softmax group 1 -- query columns 32..63
+//   warps 4-19  : softmax groups 0..3 -- query columns 16g..16g+15 (thread t <-> TMEM lane t)
 // One CTA per SM, persistent over (head, q-block) units in head-major order so a head's K/V stays
 // resident in L2.  Every mbarrier wait is bounded (bsa_ptx.cuh); a timeout records an error code
 // and the CTA winds down.
@@ -57,7 +56,14 @@ constexpr int kOffP = kOffQ + 2 * kQBytes;
 constexpr int kOffK = kOffP + kPBytes;
 constexpr int kOffV = kOffK + kKStages * kPairBytes;
 constexpr int kTileBytes = kOffV + kVSlots * kVBlockBytes;
-constexpr int kThreads = 384;
+#ifndef BSA_GROUP_COLS
+#define BSA_GROUP_COLS 16
+#endif
+constexpr int kCols = BSA_GROUP_COLS;               // query columns per softmax group
+constexpr int kGroups = 64 / kCols;                 // softmax groups (4 warps each)
+constexpr int kSoftmaxThreads = 128 * kGroups;
+constexpr int kThreads = 128 + kSoftmaxThreads;
+static_assert(kCols == 16 || kCols == 32, "softmax group width");
 constexpr float kRescaleThreshold = 8.0f;           // log2 units: P <= 2^8 between rescales
 
 // TMEM columns: S^T double buffer (64 columns each), O^T in two KV-block halves (64 columns each).
@@ -105,7 +111,7 @@ __device__ int g_attn_err;
 
 #ifdef BSA_PROFILE
 // Profiling builds only: per CTA and warp, cycles spent in up to 7 wait sites + the role's total.
-__device__ long long g_bsa_prof[1024][12][8];
+__device__ long long g_bsa_prof[1024][24][8];
 #define PACC(i) (&pacc[i])
 #define PTS_START() pts_last = clock64()
 #define PTS(i)                        \
@@ -153,12 +159,14 @@ __device__ __forceinline__ int named_bar_or(int id, int n, int pred) {
   return r;
 }
 
-// Transposed warp reduction over 32 columns: lane L holds v[0..31] (one value per column) for
-// its own key row; afterwards lane L holds the reduction over the 32 lanes of column L.
-template <bool kMax>
-__device__ __forceinline__ float transpose_reduce32(float (&v)[32], int lane) {
+// Transposed warp reduction over N columns (N = 16 or 32): lane L holds v[0..N-1] (one value per
+// column) for its own key row; afterwards lane L holds the reduction over all 32 lanes of column
+// L % N.  N-1 shuffles halve the columns held per lane; for N < 32 the remaining lane halves are
+// then combined.
+template <bool kMax, int N>
+__device__ __forceinline__ float transpose_reduce(float (&v)[N], int lane) {
 #pragma unroll
-  for (int lvl = 16; lvl >= 1; lvl >>= 1) {
+  for (int lvl = N / 2; lvl >= 1; lvl >>= 1) {
     const bool up = (lane & lvl) != 0;
 #pragma unroll
     for (int i = 0; i < lvl; ++i) {
@@ -168,7 +176,13 @@ __device__ __forceinline__ float transpose_reduce32(float (&v)[32], int lane) {
       v[i] = kMax ? fmaxf(keep, recv) : keep + recv;
     }
   }
-  return v[0];
+  float r = v[0];
+#pragma unroll
+  for (int off = N; off < 32; off <<= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, r, off);
+    r = kMax ? fmaxf(r, o) : r + o;
+  }
+  return r;
 }
 
 // Block ids of step j of a unit (the second id duplicates the first for an odd tail; those rows
@@ -220,14 +234,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ss.s_full[i], 1);
-      mbar_init(&ss.s_empty[i], 256);
+      mbar_init(&ss.s_empty[i], kSoftmaxThreads);
       mbar_init(&ss.q_full[i], 1);
       mbar_init(&ss.q_empty[i], 1);
       mbar_init(&ss.drain[i], 1);
     }
-    mbar_init(&ss.p_full, 256);
+    mbar_init(&ss.p_full, kSoftmaxThreads);
     mbar_init(&ss.p_empty, 1);
-    mbar_init(&ss.o_empty, 256);
+    mbar_init(&ss.o_empty, kSoftmaxThreads);
     ss.abort_flag = 0;
     fence_mbar_init();
   }
@@ -443,10 +457,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else
 #endif
     {
-      const int grp = (warp - 4) >> 2;        // 0: columns 0..31, 1: columns 32..63
+      const int grp = (warp - 4) >> 2;        // group g owns query columns [g*kCols, (g+1)*kCols)
       const int wq = warp & 3;                // TMEM lane quarter
       const int t = wq * 32 + lane;           // TMEM lane == key row (S^T) == d row (O^T)
-      const int c0 = grp * 32;                // first query column of this group
+      const int c0 = grp * kCols;             // first query column of this group
       const int bar_id = 1 + grp;
       const uint32_t lane_base = static_cast<uint32_t>(wq * 32) << 16;
       const float scale_log2 = p.scale_log2;
@@ -458,10 +472,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bh = unit / p.nqb;
         const int qblk = unit - bh * p.nqb;
         // mcol[c0 + q]: running max of query column c0+q (log2 domain), shared by the group
-        float l_part[32];
+        float l_part[kCols];
 #pragma unroll
-        for (int q = 0; q < 32; ++q) l_part[q] = 0.f;
-        if (t < 32) ss.mcol[c0 + t] = 0.f;
+        for (int q = 0; q < kCols; ++q) l_part[q] = 0.f;
+        if (t < kCols) ss.mcol[c0 + t] = 0.f;
         named_bar_sync(bar_id, 128);
         const float4* mvec = reinterpret_cast<const float4*>(&ss.mcol[c0]);
         for (int j = 0; j < nsteps && ok; ++j, ++g) {
@@ -471,13 +485,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           PTS_START();
           tc_fence_after();
           const bool masked = odd_tail && j == nsteps - 1 && t >= 64;
-          float x[32];  // x = S*scale*log2e - m
+          float x[kCols];  // x = S*scale*log2e - m
           {
-            uint32_t r[32];
-            tmem_ld32(tmem + lane_base + col_s(sb) + c0, r);
+            uint32_t r[kCols];
+            if (kCols == 32) tmem_ld32(tmem + lane_base + col_s(sb) + c0, r);
+            else tmem_ld16(tmem + lane_base + col_s(sb) + c0, r);
             tmem_ld_wait();
 #pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4) {
+            for (int q4 = 0; q4 < kCols / 4; ++q4) {
               const float4 mv = mvec[q4];
               const float mq[4] = {mv.x, mv.y, mv.z, mv.w};
 #pragma unroll
@@ -491,22 +506,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           // ---- lazy running max: does any key of the group exceed m + threshold?
           float mx = x[0];
 #pragma unroll
-          for (int q = 1; q < 32; ++q) mx = fmaxf(mx, x[q]);
+          for (int q = 1; q < kCols; ++q) mx = fmaxf(mx, x[q]);
           const int over = named_bar_or(bar_id, 128, (j == 0 || mx > kRescaleThreshold) ? 1 : 0);
           if (over) {
             // slow path (first step of a block, or a large jump of the max): exact column max,
             // reduced in place, then x is reloaded from TMEM (S is released only after this)
-            ss.red[wq][c0 + lane] = transpose_reduce32<true>(x, lane);
+            const float cmax = transpose_reduce<true, kCols>(x, lane);
+            if (lane < kCols) ss.red[wq][c0 + lane] = cmax;
             {
-              uint32_t r[32];
-              tmem_ld32(tmem + lane_base + col_s(sb) + c0, r);
+              uint32_t r[kCols];
+              if (kCols == 32) tmem_ld32(tmem + lane_base + col_s(sb) + c0, r);
+              else tmem_ld16(tmem + lane_base + col_s(sb) + c0, r);
               tmem_ld_wait();
 #pragma unroll
-              for (int q = 0; q < 32; ++q)
+              for (int q = 0; q < kCols; ++q)
                 x[q] = masked ? -INFINITY : fmaf(__uint_as_float(r[q]), scale_log2, -ss.mcol[c0 + q]);
             }
             named_bar_sync(bar_id, 128);
-            if (t < 32) {
+            if (t < kCols) {
               const int c = c0 + t;
               const float cm = fmaxf(fmaxf(ss.red[0][c], ss.red[1][c]), fmaxf(ss.red[2][c], ss.red[3][c]));
               // shift of column c: the new max on the first step, else only when it jumps by > 2^8
@@ -514,9 +531,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               ss.colv[c] = d;
               ss.mcol[c] += d;
             }
-            const int need = named_bar_or(bar_id, 128, (t < 32 && j > 0 && ss.colv[c0 + t] != 0.f) ? 1 : 0);
+            const int need = named_bar_or(bar_id, 128, (t < kCols && j > 0 && ss.colv[c0 + t] != 0.f) ? 1 : 0);
 #pragma unroll
-            for (int q = 0; q < 32; ++q) x[q] -= ss.colv[c0 + q];
+            for (int q = 0; q < kCols; ++q) x[q] -= ss.colv[c0 + q];
             if (need) {
               // O^T columns of this group must be rescaled: the previous step's PV must be complete
               ok = mbar_wait(&ss.p_empty, static_cast<uint32_t>((g - 1) & 1), abort_flag, err, 122, PACC(3));
@@ -524,18 +541,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               tc_fence_after();
 #pragma unroll
               for (int half = 0; half < 2; ++half) {
-                uint32_t r[32];
-                const uint32_t a = tmem + lane_base + kColO + half * 64 + c0;
-                tmem_ld32(a, r);
-                tmem_ld_wait();
 #pragma unroll
-                for (int q = 0; q < 32; ++q)
-                  r[q] = __float_as_uint(__uint_as_float(r[q]) * ex2_approx(-ss.colv[c0 + q]));
-                tmem_st32(a, r);
+                for (int c = 0; c < kCols; c += 16) {
+                  uint32_t r[16];
+                  const uint32_t a = tmem + lane_base + kColO + half * 64 + c0 + c;
+                  tmem_ld16(a, r);
+                  tmem_ld_wait();
+#pragma unroll
+                  for (int q = 0; q < 16; ++q)
+                    r[q] = __float_as_uint(__uint_as_float(r[q]) * ex2_approx(-ss.colv[c0 + c + q]));
+                  tmem_st16(a, r);
+                }
               }
               tmem_st_wait();
 #pragma unroll
-              for (int q = 0; q < 32; ++q) l_part[q] *= ex2_approx(-ss.colv[c0 + q]);
+              for (int q = 0; q < kCols; ++q) l_part[q] *= ex2_approx(-ss.colv[c0 + q]);
             }
             named_bar_sync(bar_id, 128);  // colv is rewritten by the next slow path
           }
@@ -543,9 +563,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&ss.s_empty[sb]);
           PTS(5);
           // ---- probabilities, row-sum partials, P^T row into the P buffer
-          uint32_t packed[16];
+          uint32_t packed[kCols / 2];
 #pragma unroll
-          for (int q = 0; q < 32; q += 2) {
+          for (int q = 0; q < kCols; q += 2) {
             const float p0 = ex2_approx(x[q]);
             const float p1 = ex2_approx(x[q + 1]);
             l_part[q] += p0;
@@ -559,9 +579,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           PTS_START();
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < kCols / 8; ++c) {
             const uint4 v = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-            *reinterpret_cast<uint4*>(sP + sw128_offset(static_cast<uint32_t>(t), static_cast<uint32_t>(grp * 4 + c))) = v;
+            *reinterpret_cast<uint4*>(sP + sw128_offset(static_cast<uint32_t>(t), static_cast<uint32_t>(c0 / 8 + c))) = v;
           }
           fence_proxy_async_smem();
           tc_fence_before();
@@ -569,24 +589,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           PTS(3);
         }
         if (!ok) break;
-        // ---- epilogue: row sums, O^T / l -> out (this group's 32 query rows)
-        ss.red[wq][c0 + lane] = transpose_reduce32<false>(l_part, lane);
+        // ---- epilogue: row sums, O^T / l -> out (this group's query rows)
+        {
+          const float lsum = transpose_reduce<false, kCols>(l_part, lane);
+          if (lane < kCols) ss.red[wq][c0 + lane] = lsum;
+        }
         ok = mbar_wait(&ss.p_empty, static_cast<uint32_t>((g - 1) & 1), abort_flag, err, 123, PACC(2));
         if (!ok) break;
         tc_fence_after();
-        float o[32];
-        {
-          uint32_t ra[32], rb[32];
-          tmem_ld32(tmem + lane_base + kColO + c0, ra);
-          tmem_ld32(tmem + lane_base + kColO + 64 + c0, rb);
+        float o[kCols];
+#pragma unroll
+        for (int c = 0; c < kCols; c += 16) {
+          uint32_t ra[16], rb[16];
+          tmem_ld16(tmem + lane_base + kColO + c0 + c, ra);
+          tmem_ld16(tmem + lane_base + kColO + 64 + c0 + c, rb);
           tmem_ld_wait();
 #pragma unroll
-          for (int q = 0; q < 32; ++q) o[q] = __uint_as_float(ra[q]) + __uint_as_float(rb[q]);
+          for (int q = 0; q < 16; ++q) o[c + q] = __uint_as_float(ra[q]) + __uint_as_float(rb[q]);
         }
         tc_fence_before();
         mbar_arrive(&ss.o_empty);
         named_bar_sync(bar_id, 128);
-        if (t < 32) {
+        if (t < kCols) {
           const int c = c0 + t;
           const float l = ss.red[0][c] + ss.red[1][c] + ss.red[2][c] + ss.red[3][c];
           ss.colv[c] = l > 0.f ? 1.f / l : 0.f;
@@ -600,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const long long base = b * p.out_sb + h * p.out_sh + t;
           const int cHW = p.cH * p.cW;
 #pragma unroll
-          for (int q = 0; q < 32; ++q) {
+          for (int q = 0; q < kCols; ++q) {
             const int r = c0 + q;
             const int ct = r / cHW;
             const int rem = r - ct * cHW;
