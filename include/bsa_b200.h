@@ -107,6 +107,25 @@ int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, i
                 int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot, void* scratch,
                 int32_t* block_indices, void* out, const int64_t* out_strides, void* stream);
 
+/* bsa_forward without caller-provided scratch -- no counterpart in the reference (MLX manages
+ * memory itself); it exists for callers that cannot allocate device memory where they call
+ * attention (a region whose memory is fixed in advance, an embedder that owns the whole device
+ * budget, a host binding without a device allocator).  Same arguments and results as bsa_forward
+ * minus `scratch`: the pooled Q/K scratch comes from an array compiled into the library, of
+ * BSA_NOALLOC_SCRATCH_BYTES per GPU that loads the library, held until the process exits.
+ * Calls that would need more (bsa_forward_scratch_bytes() > BSA_NOALLOC_SCRATCH_BYTES) return
+ * BSA_ERR_SHAPE.  Nothing is allocated: no cudaMalloc, cudaFree or allocating library routine.
+ * The first call on a device resolves the array's device address (cudaGetSymbolAddress, with that
+ * device current); make that first call before any stream capture.  Every call on a device shares
+ * the one array: calls whose kernels overlap on the GPU (different streams, or concurrent host
+ * threads) race on it and must be serialised by the caller. */
+#define BSA_NOALLOC_SCRATCH_BYTES (16u << 20)
+int bsa_forward_noalloc(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
+                        const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl,
+                        int Wl, int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt,
+                        int rope_dh, int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot,
+                        int32_t* block_indices, void* out, const int64_t* out_strides, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

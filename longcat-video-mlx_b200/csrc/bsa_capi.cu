@@ -106,6 +106,16 @@ int check_pool_args(const void* x, int dtype, int B, int H, int S, int D, int64_
 
 }  // namespace
 
+namespace bsa {
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+}  // namespace bsa
+
 extern "C" {
 
 int bsa_version(void) { return 100; }

@@ -50,4 +50,7 @@ int launch_attn(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensor
 int attn_device_error(int clear);
 int score_device_error(int clear);
 
+// Record the calling host thread's error message (read back by bsa_last_error); returns `code`.
+int set_error(int code, const char* fmt, ...);
+
 }  // namespace bsa
