@@ -69,8 +69,8 @@ int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t 
 /* block_routing_scores + topk_block_indices -- block_sparse_attention.py:107-134.
  * score[i][j] = fp32 fma chain over d = 0..D-1 of q_pooled[i][d] * k_pooled[j][d]; each row
  * keeps the topk largest scores (ties: smaller block id first) and writes their block ids
- * sorted ascending.  scores (nullable) receives the full [BH, nb, nb] score matrix instead of
- * being kept on chip (only for small problems / the score API). */
+ * sorted ascending.  scores (required, caller-owned, 16-byte aligned) receives the full
+ * [BH, nb, nb] fp32 score matrix that the selection reads.  D must be a multiple of 8. */
 int bsa_score_topk(const float* q_pooled, const float* k_pooled, int BH, int nb, int D, int topk,
                    int32_t* block_indices, float* scores, void* stream);
 
@@ -97,7 +97,8 @@ int bsa_attention_indices(const void* q, const void* k, const void* v, const int
 /* Full BSA call -- bsa_attention(q, k, v, shape, sparsity, chunk_thw, sm_scale),
  * block_sparse_attention.py:201-250: pool Q and K, score, top-k, sparse attention.
  * scratch: caller-provided device memory of bsa_forward_scratch_bytes() bytes (pooled fp32
- * Q/K).  block_indices receives the routing ([B,H,nb,topk]).  With rope != NULL, q and k are
+ * Q/K, [B*H, nb, D] each, then the fp32 block-score matrix [B*H, nb, nb] with rows padded to a
+ * multiple of 4).  block_indices receives the routing ([B,H,nb,topk]).  With rope != NULL, q and k are
  * pre-RoPE and q_rot / k_rot (contiguous [B,H,S,D]) receive the rotated tensors that the
  * attention then reads. */
 int64_t bsa_forward_scratch_bytes(int B, int H, int S, int D, int cT, int cH, int cW);
@@ -111,7 +112,7 @@ int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, i
  * memory itself); it exists for callers that cannot allocate device memory where they call
  * attention (a region whose memory is fixed in advance, an embedder that owns the whole device
  * budget, a host binding without a device allocator).  Same arguments and results as bsa_forward
- * minus `scratch`: the pooled Q/K scratch comes from an array compiled into the library, of
+ * minus `scratch`: the pooled Q/K and score scratch comes from an array compiled into the library, of
  * BSA_NOALLOC_SCRATCH_BYTES per GPU that loads the library, held until the process exits.
  * Calls that would need more (bsa_forward_scratch_bytes() > BSA_NOALLOC_SCRATCH_BYTES) return
  * BSA_ERR_SHAPE.  Nothing is allocated: no cudaMalloc, cudaFree or allocating library routine.

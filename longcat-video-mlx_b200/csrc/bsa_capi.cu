@@ -163,35 +163,36 @@ int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t 
 
 int bsa_score_topk(const float* q_pooled, const float* k_pooled, int BH, int nb, int D, int topk,
                    int32_t* block_indices, float* scores, void* stream) {
-  if (!q_pooled || !k_pooled || !block_indices) return fail(BSA_ERR_ARG, "null pointer");
-  if (BH <= 0 || nb <= 0 || D <= 0 || D > 128 || D % 4)
-    return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nb=%d D=%d (D must be a multiple of 4, at most 128)", BH, nb, D);
+  if (!q_pooled || !k_pooled || !block_indices || !scores) return fail(BSA_ERR_ARG, "null pointer");
+  if (BH <= 0 || nb <= 0 || D <= 0 || D > 128 || D % 8)
+    return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nb=%d D=%d (D must be a multiple of 8, at most 128)", BH, nb, D);
+  if (reinterpret_cast<uintptr_t>(scores) & 15u) return fail(BSA_ERR_ALIGN, "scores must be 16-byte aligned");
   if ((reinterpret_cast<uintptr_t>(q_pooled) | reinterpret_cast<uintptr_t>(k_pooled)) & 15u)
     return fail(BSA_ERR_ALIGN, "pooled blocks must be 16-byte aligned");
   if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
   bsa::ScoreArgs a;
   a.qp = q_pooled; a.kp = k_pooled; a.BH = BH; a.nq = nb; a.nk = nb; a.D = D; a.topk = topk;
-  a.idx = block_indices; a.scores = scores; a.scores_in = nullptr;
+  a.idx = block_indices; a.scores = scores; a.ldc = nb;
   const int rc = bsa::launch_score_topk(a, static_cast<cudaStream_t>(stream));
   if (rc == BSA_ERR_CUDA) return cuda_fail("score/top-k kernel launch");
-  if (rc) return fail(rc, "score/top-k: %d KV blocks do not fit the on-chip score rows", nb);
+  if (rc) return fail(rc, "score/top-k: unsupported sizes (nb=%d)", nb);
   return BSA_OK;
 }
 
 int bsa_block_scores(const float* q_pooled, const float* k_pooled, int BH, int nq, int nk, int D, float* scores,
                      void* stream) {
   if (!q_pooled || !k_pooled || !scores) return fail(BSA_ERR_ARG, "null pointer");
-  if (BH <= 0 || nq <= 0 || nk <= 0 || D <= 0 || D > 128 || D % 4)
-    return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nq=%d nk=%d D=%d (D must be a multiple of 4, at most 128)", BH, nq,
+  if (BH <= 0 || nq <= 0 || nk <= 0 || D <= 0 || D > 128 || D % 8)
+    return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nq=%d nk=%d D=%d (D must be a multiple of 8, at most 128)", BH, nq,
                 nk, D);
   if ((reinterpret_cast<uintptr_t>(q_pooled) | reinterpret_cast<uintptr_t>(k_pooled)) & 15u)
     return fail(BSA_ERR_ALIGN, "pooled blocks must be 16-byte aligned");
   bsa::ScoreArgs a;
   a.qp = q_pooled; a.kp = k_pooled; a.BH = BH; a.nq = nq; a.nk = nk; a.D = D; a.topk = 1;
-  a.idx = nullptr; a.scores = scores; a.scores_in = nullptr;
+  a.idx = nullptr; a.scores = scores; a.ldc = nk;
   const int rc = bsa::launch_scores_only(a, static_cast<cudaStream_t>(stream));
   if (rc == BSA_ERR_CUDA) return cuda_fail("score kernel launch");
-  if (rc) return fail(rc, "scores: %d KV blocks do not fit the on-chip score rows", nk);
+  if (rc) return fail(rc, "scores: unsupported sizes (nq=%d nk=%d)", nq, nk);
   return BSA_OK;
 }
 
@@ -199,12 +200,9 @@ int bsa_topk_from_scores(const float* scores, int rows, int nk, int topk, int32_
   if (!scores || !block_indices) return fail(BSA_ERR_ARG, "null pointer");
   if (rows <= 0 || nk <= 0) return fail(BSA_ERR_SHAPE, "bad sizes rows=%d nk=%d", rows, nk);
   if (topk < 1 || topk > nk) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nk);
-  bsa::ScoreArgs a;
-  a.qp = nullptr; a.kp = nullptr; a.BH = 1; a.nq = rows; a.nk = nk; a.D = 1; a.topk = topk;
-  a.idx = block_indices; a.scores = nullptr; a.scores_in = scores;
-  const int rc = bsa::launch_score_topk(a, static_cast<cudaStream_t>(stream));
+  const int rc = bsa::launch_topk(scores, rows, nk, nk, topk, block_indices, static_cast<cudaStream_t>(stream));
   if (rc == BSA_ERR_CUDA) return cuda_fail("top-k kernel launch");
-  if (rc) return fail(rc, "top-k: %d KV blocks do not fit the on-chip score rows", nk);
+  if (rc) return fail(rc, "top-k: unsupported sizes (nk=%d)", nk);
   return BSA_OK;
 }
 
@@ -241,10 +239,15 @@ int bsa_attention_indices(const void* q, const void* k, const void* v, const int
   return rc;
 }
 
+namespace {
+int64_t score_ld(int nb) { return (static_cast<int64_t>(nb) + 3) & ~int64_t(3); }
+}  // namespace
+
 int64_t bsa_forward_scratch_bytes(int B, int H, int S, int D, int cT, int cH, int cW) {
   const int n = cT * cH * cW;
   if (n <= 0 || B <= 0 || H <= 0 || S <= 0 || D <= 0) return 0;
-  return 2ll * B * H * (S / n) * D * 4;
+  const int64_t nb = S / n;
+  return 2ll * B * H * nb * D * 4 + static_cast<int64_t>(B) * H * nb * score_ld(static_cast<int>(nb)) * 4;
 }
 
 int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
@@ -271,8 +274,17 @@ int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, i
   rc = bsa_mean_pool(k, dtype, B, H, S, D, k_strides[0], k_strides[1], k_strides[2], T, Hl, Wl, cT, cH, cW, rope,
                      rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, k_rot, kp, stream);
   if (rc) return rc;
-  rc = bsa_score_topk(qp, kp, B * H, nb, D, topk, block_indices, nullptr, stream);
-  if (rc) return rc;
+  {
+    if (D % 8) return fail(BSA_ERR_SHAPE, "head_dim D=%d must be a multiple of 8", D);
+    if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
+    bsa::ScoreArgs a;
+    a.qp = qp; a.kp = kp; a.BH = B * H; a.nq = nb; a.nk = nb; a.D = D; a.topk = topk;
+    a.idx = block_indices; a.ldc = static_cast<int>(score_ld(nb));
+    a.scores = kp + static_cast<int64_t>(B) * H * nb * D;
+    rc = bsa::launch_score_topk(a, static_cast<cudaStream_t>(stream));
+    if (rc == BSA_ERR_CUDA) return cuda_fail("score/top-k kernel launch");
+    if (rc) return fail(rc, "score/top-k: unsupported sizes (nb=%d)", nb);
+  }
   if (rope) {
     const int64_t cst[3] = {static_cast<int64_t>(H) * S * D, static_cast<int64_t>(S) * D, D};
     return bsa_attention_indices(q_rot, k_rot, v, block_indices, dtype, B, H, S, D, cst, cst, v_strides, T, Hl, Wl,

@@ -25,15 +25,16 @@ int launch_pool(const PoolArgs& a, cudaStream_t stream);
 
 // ------------------------------------------------------------------ block scores + top-k
 struct ScoreArgs {
-  const float* qp;       // [BH, nb, D] fp32
+  const float* qp;       // [BH, nq, D] fp32
   const float* kp;       // [BH, nk, D] fp32
   int BH, nq, nk, D, topk;
-  int32_t* idx;          // [BH, nb, topk], ascending block ids
-  float* scores;         // nullable: [BH, nq, nk] fp32 output (routing-score API)
-  const float* scores_in;  // nullable: select from these scores instead of computing them
+  int32_t* idx;          // [BH, nq, topk], ascending block ids
+  float* scores;         // [BH, nq, ldc] fp32 (output of the score GEMM, input of the top-k)
+  int ldc;               // row stride of `scores` (>= nk)
 };
 int launch_score_topk(const ScoreArgs& a, cudaStream_t stream);
 int launch_scores_only(const ScoreArgs& a, cudaStream_t stream);
+int launch_topk(const float* scores, int rows, int nk, int ldc, int topk, int32_t* idx, cudaStream_t stream);
 
 // ------------------------------------------------------------------ sparse attention
 struct AttnArgs {

@@ -243,242 +243,284 @@ int launch_pool(const PoolArgs& a, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
 }
 
-// ======================================================================== scores + top-k
-namespace score {
+// ======================================================================== block scores
+// score[bh][i][j] = fp32 fma chain over d = 0..D-1 of qp[bh][i][d] * kp[bh][j][d], starting at 0.
+// SGEMM-style tiling: a 128x128 tile per CTA, 8x8 scores per thread (two 4x4 quadrants), K in
+// chunks of 8 through double-buffered shared memory.  Each score still accumulates over d in
+// ascending order, so it is the same fp32 value the oracle computes with C fmaf.
+namespace gemm {
 constexpr int kThreads = 256;
-constexpr int kJT = 64;          // key blocks per shared-memory chunk
-constexpr int kMaxD = 128;
+constexpr int kTile = 128;
+constexpr int kBK = 8;
+constexpr int kLd = kTile + 4;  // padded smem row (floats)
+
+struct Args {
+  const float* qp;   // [BH, nq, D]
+  const float* kp;   // [BH, nk, D]
+  float* scores;     // [BH, nq, ldc]
+  int nq, nk, D, ldc;
+};
+
+__global__ void __launch_bounds__(kThreads, 2) score_gemm_kernel(Args a) {
+  __shared__ __align__(16) float As[2][kBK][kLd];
+  __shared__ __align__(16) float Bs[2][kBK][kLd];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int bh = blockIdx.z;
+  const int i0 = blockIdx.y * kTile, j0 = blockIdx.x * kTile;
+  const float* qp = a.qp + static_cast<long long>(bh) * a.nq * a.D;
+  const float* kp = a.kp + static_cast<long long>(bh) * a.nk * a.D;
+  // global -> smem staging map: thread stages row (tid >> 1), d4 = (tid & 1) of each operand
+  const int srow = tid >> 1, sd4 = tid & 1;
+  const bool qv = i0 + srow < a.nq, kv = j0 + srow < a.nk;
+  const float* qsrc = qp + static_cast<long long>(i0 + srow) * a.D + 4 * sd4;
+  const float* ksrc = kp + static_cast<long long>(j0 + srow) * a.D + 4 * sd4;
+  float acc[8][8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[r][c] = 0.f;
+  const int nchunks = a.D / kBK;
+  float4 qn = qv ? __ldg(reinterpret_cast<const float4*>(qsrc)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 kn = kv ? __ldg(reinterpret_cast<const float4*>(ksrc)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int ch = 0; ch < nchunks; ++ch) {
+    const int buf = ch & 1;
+    As[buf][4 * sd4 + 0][srow] = qn.x;
+    As[buf][4 * sd4 + 1][srow] = qn.y;
+    As[buf][4 * sd4 + 2][srow] = qn.z;
+    As[buf][4 * sd4 + 3][srow] = qn.w;
+    Bs[buf][4 * sd4 + 0][srow] = kn.x;
+    Bs[buf][4 * sd4 + 1][srow] = kn.y;
+    Bs[buf][4 * sd4 + 2][srow] = kn.z;
+    Bs[buf][4 * sd4 + 3][srow] = kn.w;
+    __syncthreads();
+    if (ch + 1 < nchunks) {  // prefetch the next chunk while this one is multiplied
+      qn = qv ? __ldg(reinterpret_cast<const float4*>(qsrc + (ch + 1) * kBK)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      kn = kv ? __ldg(reinterpret_cast<const float4*>(ksrc + (ch + 1) * kBK)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int d = 0; d < kBK; ++d) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][d][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][d][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][d][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][d][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[r][c] = __fmaf_rn(av[r], bv[c], acc[r][c]);
+    }
+  }
+  float* out = a.scores + static_cast<long long>(bh) * a.nq * a.ldc;
+  const bool vec = (a.ldc & 3) == 0;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const int i = i0 + (r < 4 ? ty * 4 + r : 64 + ty * 4 + (r - 4));
+    if (i >= a.nq) continue;
+    float* orow = out + static_cast<long long>(i) * a.ldc;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = j0 + h * 64 + tx * 4;
+      if (vec && j + 3 < a.nk) {
+        *reinterpret_cast<float4*>(orow + j) =
+            make_float4(acc[r][4 * h], acc[r][4 * h + 1], acc[r][4 * h + 2], acc[r][4 * h + 3]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (j + c < a.nk) orow[j + c] = acc[r][4 * h + c];
+      }
+    }
+  }
+}
+}  // namespace gemm
+
+// ======================================================================== top-k per row
+// One warp per score row.  The k-th largest key T is found by a binary search over the 32-bit
+// order-preserving keys (warp-wide counts, no shared-memory atomics); the row is then scanned in
+// ascending block order taking every key above T and the first `need` keys equal to T.
+namespace topk {
+constexpr int kThreads = 256;
 
 __device__ __forceinline__ uint32_t ordered_key(float s) {
-  // -0.0 and +0.0 are one score; NaN sorts below everything
-  if (s != s) return 0u;
+  // -0.0 and +0.0 are one score; NaN sorts below every number (key 1); key 0 marks padding
+  if (s != s) return 1u;
   const uint32_t u = __float_as_uint(s == 0.0f ? 0.0f : s);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
 struct Args {
-  const float* sin;  // when set: select from these scores [BH, nq, nk] instead of computing them
-  const float* qp;
-  const float* kp;
-  int BH, nq, nk, D, topk, QT;
-  int32_t* idx;
-  float* scores;
-  int select;  // 0: write scores only
+  const float* scores;  // rows of length nk, stride ldc
+  int rows, nk, ldc, topk;
+  int32_t* idx;         // [rows, topk]
 };
 
-// smem: [QT][nk] scores | union{ qT[D][QT] + kT[D][kJT] , per-warp histograms 8 x 256 }
-__global__ void __launch_bounds__(kThreads) score_topk_kernel(Args a) {
-  extern __shared__ __align__(16) float sm[];
-  float* srow = sm;                                             // QT * nk
-  float* qT = sm + static_cast<size_t>(a.QT) * a.nk;            // D * QT
-  float* kT = qT + kMaxD * a.QT;                                // D * kJT
-  uint32_t* hist = reinterpret_cast<uint32_t*>(qT);             // 8 * 256 (after scoring)
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
-  const int tiles_per_head = (a.nq + a.QT - 1) / a.QT;
-  const int bh = blockIdx.x / tiles_per_head;
-  const int q0 = (blockIdx.x - bh * tiles_per_head) * a.QT;
-  const int qn = min(a.QT, a.nq - q0);
-  const float* qp = a.qp + (static_cast<long long>(bh) * a.nq + q0) * a.D;
-  const float* kp = a.kp + static_cast<long long>(bh) * a.nk * a.D;
-  if (a.sin) {
-    for (int e = tid; e < qn * a.nk; e += kThreads) {
-      const int i = e / a.nk, j = e - i * a.nk;
-      srow[static_cast<size_t>(i) * a.nk + j] = a.sin[(static_cast<long long>(bh) * a.nq + q0 + i) * a.nk + j];
-    }
-  } else {
-    // ---- stage the q tile transposed: qT[d][i ^ qswz(d)] (coalesced float4 reads; the XOR
-    //      keeps groups of 4 queries contiguous and spreads the transposed stores over banks)
-    const int D4 = a.D >> 2;
-    const int qmask = (a.QT >> 2) - 1;
-    for (int e = tid; e < a.QT * D4; e += kThreads) {
-      const int i = e / D4, d4 = e - i * D4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (i < qn) v = __ldg(reinterpret_cast<const float4*>(qp + static_cast<long long>(i) * a.D) + d4);
-      const int col = i ^ ((d4 & qmask) << 2);
-      qT[(4 * d4 + 0) * a.QT + col] = v.x;
-      qT[(4 * d4 + 1) * a.QT + col] = v.y;
-      qT[(4 * d4 + 2) * a.QT + col] = v.z;
-      qT[(4 * d4 + 3) * a.QT + col] = v.w;
-    }
-    // thread tile: 4 query rows x 2 key blocks
-    const int ngroups = a.QT / 4;
-    const int qg = tid / 32;         // query group (4 rows)
-    const int jp = tid & 31;         // key pair inside the chunk
-    const bool active = qg < ngroups;
-    for (int j0 = 0; j0 < a.nk; j0 += kJT) {
-      const int jn = min(kJT, a.nk - j0);
-      __syncthreads();
-      // kT[d][j ^ kswz(d)], kswz even so key pairs (2p, 2p+1) stay contiguous
-      for (int e = tid; e < kJT * D4; e += kThreads) {
-        const int j = e / D4, d4 = e - j * D4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (j < jn) v = __ldg(reinterpret_cast<const float4*>(kp + static_cast<long long>(j0 + j) * a.D) + d4);
-        const int col = j ^ ((d4 & 15) << 1);
-        kT[(4 * d4 + 0) * kJT + col] = v.x;
-        kT[(4 * d4 + 1) * kJT + col] = v.y;
-        kT[(4 * d4 + 2) * kJT + col] = v.z;
-        kT[(4 * d4 + 3) * kJT + col] = v.w;
-      }
-      __syncthreads();
-      if (active) {
-        float acc[4][2];
-  #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = 0.f;
-  #pragma unroll 8
-        for (int d = 0; d < a.D; ++d) {
-          const int d4 = d >> 2;
-          const float4 qv = *reinterpret_cast<const float4*>(qT + d * a.QT + ((qg * 4) ^ ((d4 & qmask) << 2)));
-          const float2 kv = *reinterpret_cast<const float2*>(kT + d * kJT + ((jp * 2) ^ ((d4 & 15) << 1)));
-          acc[0][0] = __fmaf_rn(qv.x, kv.x, acc[0][0]);
-          acc[0][1] = __fmaf_rn(qv.x, kv.y, acc[0][1]);
-          acc[1][0] = __fmaf_rn(qv.y, kv.x, acc[1][0]);
-          acc[1][1] = __fmaf_rn(qv.y, kv.y, acc[1][1]);
-          acc[2][0] = __fmaf_rn(qv.z, kv.x, acc[2][0]);
-          acc[2][1] = __fmaf_rn(qv.z, kv.y, acc[2][1]);
-          acc[3][0] = __fmaf_rn(qv.w, kv.x, acc[3][0]);
-          acc[3][1] = __fmaf_rn(qv.w, kv.y, acc[3][1]);
-        }
-  #pragma unroll
-        for (int i = 0; i < 4; ++i)
-  #pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            const int j = jp * 2 + jj;
-            if (j < jn) srow[static_cast<size_t>(qg * 4 + i) * a.nk + j0 + j] = acc[i][jj];
-          }
-      }
-    }
-  }
-  __syncthreads();
-  if (a.scores) {
-    for (int e = tid; e < qn * a.nk; e += kThreads) {
-      const int i = e / a.nk, j = e - i * a.nk;
-      a.scores[(static_cast<long long>(bh) * a.nq + q0 + i) * a.nk + j] = srow[static_cast<size_t>(i) * a.nk + j];
-    }
-  }
-  if (!a.select) return;
-  // ---- top-k per row: radix select on ordered keys (4 x 8-bit digits), one warp per row
-  uint32_t* h = hist + warp * 256;
-  const uint32_t lt_mask = (1u << lane) - 1u;
-  for (int i = warp; i < qn; i += kThreads / 32) {
-    const float* row = srow + static_cast<size_t>(i) * a.nk;
-    uint32_t prefix = 0, pmask = 0;
-    int need = a.topk;  // keys still to take among those matching prefix
-#pragma unroll 1
-    for (int shift = 24; shift >= 0; shift -= 8) {
+// PL > 0: the row lives in registers (PL keys per lane, nk <= 32*PL); PL == 0: re-read from memory
+template <int PL>
+__global__ void __launch_bounds__(kThreads) topk_kernel(Args a) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+  if (row >= a.rows) return;
+  const float* src = a.scores + static_cast<long long>(row) * a.ldc;
+  const int nk = a.nk, k = a.topk;
+  uint32_t key[PL > 0 ? PL : 1];
+  if (PL > 0) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) h[lane * 8 + e] = 0;
+    for (int e = 0; e < PL; ++e) {
+      const int j = lane + 32 * e;
+      key[e] = j < nk ? ordered_key(__ldg(src + j)) : 0u;
+    }
+  }
+  // number of keys >= t (t >= 1, so padding keys of 0 never count)
+  auto count_ge = [&](uint32_t t) -> int {
+    int c = 0;
+    if (PL > 0) {
+#pragma unroll
+      for (int e = 0; e < (PL > 0 ? PL : 1); ++e) c += key[e] >= t ? 1 : 0;
+    } else {
+      for (int j = lane; j < nk; j += 32) c += ordered_key(__ldg(src + j)) >= t ? 1 : 0;
+    }
+    return __reduce_add_sync(0xffffffffu, c);
+  };
+  uint32_t T;
+  int need;
+  if constexpr (PL > 0) {
+    // Radix select: 8-bit digits, starting below the bits that every key of the row shares
+    // (from the row's min and max key), counted in a per-warp shared histogram.
+    __shared__ __align__(16) uint32_t hist_all[kThreads / 32][256];
+    uint32_t* h = hist_all[threadIdx.x >> 5];
+    uint32_t kmin = 0xffffffffu, kmax = 0u;
+#pragma unroll
+    for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
+      if (key[e] != 0u) {
+        kmin = min(kmin, key[e]);
+        kmax = max(kmax, key[e]);
+      }
+    }
+    kmin = __reduce_min_sync(0xffffffffu, kmin);
+    kmax = __reduce_max_sync(0xffffffffu, kmax);
+    int shift = 32 - __clz(kmin ^ kmax);  // low bits that still vary across the row
+    uint32_t prefix = shift >= 32 ? 0u : (kmax & ~((1u << shift) - 1u));
+    need = k;
+    while (shift > 0) {
+      const int w = shift < 8 ? shift : 8;
+      const int hi_bits = shift;  // keys must match `prefix` above bit `shift`
+      shift -= w;
+      const uint32_t dmask = (1u << w) - 1u;
+      reinterpret_cast<uint4*>(h)[lane * 2] = make_uint4(0u, 0u, 0u, 0u);
+      reinterpret_cast<uint4*>(h)[lane * 2 + 1] = make_uint4(0u, 0u, 0u, 0u);
       __syncwarp();
-      for (int j = lane; j < a.nk; j += 32) {
-        const uint32_t u = ordered_key(row[j]);
-        if ((u & pmask) == prefix) atomicAdd(&h[(u >> shift) & 255u], 1u);
+#pragma unroll
+      for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
+        const uint32_t u = key[e];
+        const bool match = u != 0u && (hi_bits >= 32 || (u >> hi_bits) == (prefix >> hi_bits));
+        if (match) atomicAdd(&h[(u >> shift) & dmask], 1u);
       }
       __syncwarp();
-      // lane L owns digits 8L .. 8L+7; suffix sums from the top digit down
-      uint32_t cnt[8];
+      const uint4 c0 = reinterpret_cast<const uint4*>(h)[lane * 2];
+      const uint4 c1 = reinterpret_cast<const uint4*>(h)[lane * 2 + 1];
+      const uint32_t cnt[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
       uint32_t tot = 0;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        cnt[e] = h[lane * 8 + e];
-        tot += cnt[e];
-      }
-      // inclusive suffix scan over lanes (lanes above contribute)
-      uint32_t suf = tot;
+      for (int b = 0; b < 8; ++b) tot += cnt[b];
+      uint32_t suf = tot;  // inclusive suffix sum over lanes >= this lane
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
-        const uint32_t v = __shfl_down_sync(0xffffffffu, suf, off);
-        if (lane + off < 32) suf += v;
+        const uint32_t o = __shfl_down_sync(0xffffffffu, suf, off);
+        if (lane + off < 32) suf += o;
       }
-      const uint32_t above = suf - tot;  // keys with digit in lanes > L
-      // the digit lane: above < need <= suf
+      const uint32_t above = suf - tot;
       const bool mine = above < static_cast<uint32_t>(need) && static_cast<uint32_t>(need) <= suf;
       int digit = 0;
       uint32_t gt = 0;
       if (mine) {
         uint32_t run = above;
 #pragma unroll
-        for (int e = 7; e >= 0; --e) {
-          if (run + cnt[e] >= static_cast<uint32_t>(need)) {
-            digit = lane * 8 + e;
+        for (int b = 7; b >= 0; --b) {
+          if (run + cnt[b] >= static_cast<uint32_t>(need)) {
+            digit = lane * 8 + b;
             gt = run;
             break;
           }
-          run += cnt[e];
+          run += cnt[b];
         }
       }
-      const uint32_t ball = __ballot_sync(0xffffffffu, mine);
-      const int src = __ffs(ball) - 1;
+      const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
       digit = __shfl_sync(0xffffffffu, digit, src);
       gt = __shfl_sync(0xffffffffu, gt, src);
       prefix |= static_cast<uint32_t>(digit) << shift;
-      pmask |= 255u << shift;
       need -= static_cast<int>(gt);
       __syncwarp();
     }
-    // prefix is now the key of the k-th largest score; take every key above it and the first
-    // `need` keys equal to it in ascending block order
-    int32_t* out = a.idx + (static_cast<long long>(bh) * a.nq + q0 + i) * a.topk;
-    int taken = 0, ties = 0;
-    for (int j0 = 0; j0 < a.nk; j0 += 32) {
-      const int j = j0 + lane;
-      const uint32_t u = j < a.nk ? ordered_key(row[j]) : 0u;
-      const bool valid = j < a.nk;
-      const bool eq = valid && u == prefix;
-      const uint32_t eqb = __ballot_sync(0xffffffffu, eq);
-      const int rank = ties + __popc(eqb & lt_mask);
-      const bool sel = valid && (u > prefix || (eq && rank < need));
-      const uint32_t sb = __ballot_sync(0xffffffffu, sel);
-      if (sel) out[taken + __popc(sb & lt_mask)] = j;
-      taken += __popc(sb);
-      ties += __popc(eqb);
+    T = prefix;
+  } else {
+    // rows too long for registers: binary search for the largest T with #(key >= T) >= k
+    // (every real key is >= 1), re-reading the row from memory
+    uint32_t lo = 1u, hi = 0xffffffffu;
+    while (lo < hi) {
+      const uint32_t mid = lo + ((hi - lo) >> 1) + 1u;
+      if (count_ge(mid) >= k) lo = mid;
+      else hi = mid - 1u;
     }
-    if (lane == 0 && taken != a.topk) atomicCAS(&g_score_err, 0, 201);
+    T = lo;
+    need = k - count_ge(T + (T != 0xffffffffu ? 1u : 0u)) * (T != 0xffffffffu ? 1 : 0);
   }
+  int32_t* out = a.idx + static_cast<long long>(row) * k;
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  int taken = 0, ties = 0;
+  auto emit = [&](uint32_t u, int j) {
+    const bool valid = j < nk;
+    const bool eq = valid && u == T;
+    const uint32_t eqb = __ballot_sync(0xffffffffu, eq);
+    const int rank = ties + __popc(eqb & lt_mask);
+    const bool sel = valid && (u > T || (eq && rank < need));
+    const uint32_t sb = __ballot_sync(0xffffffffu, sel);
+    if (sel) out[taken + __popc(sb & lt_mask)] = j;
+    taken += __popc(sb);
+    ties += __popc(eqb);
+  };
+  if (PL > 0) {
+#pragma unroll
+    for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
+      if (32 * e >= nk) break;  // warp-uniform
+      emit(key[e], lane + 32 * e);
+    }
+  } else {
+    for (int j0 = 0; j0 < nk; j0 += 32) {
+      const int j = j0 + lane;
+      emit(j < nk ? ordered_key(__ldg(src + j)) : 0u, j);
+    }
+  }
+  if (lane == 0 && taken != k) atomicCAS(&g_score_err, 0, 201);
 }
+}  // namespace topk
 
-int pick_qt(int nk, int nq) {
-  const int budget = 232448 - 2048;
-  int qt = 32;
-  while (qt > 4) {
-    const size_t bytes = static_cast<size_t>(qt) * nk * 4 + static_cast<size_t>(kMaxD) * (qt + kJT) * 4;
-    if (bytes <= static_cast<size_t>(budget)) break;
-    qt >>= 1;
-  }
-  (void)nq;
-  return qt;
-}
-
-int launch(const ScoreArgs& s, int select, cudaStream_t stream) {
-  Args a;
-  const int nq = s.nq;
-  a.sin = s.scores_in;
-  a.qp = s.qp; a.kp = s.kp; a.BH = s.BH; a.nq = nq; a.nk = s.nk; a.D = s.D; a.topk = s.topk;
-  a.idx = s.idx; a.scores = s.scores; a.select = select;
-  if (!s.scores_in && (s.D > kMaxD || s.D < 1)) return BSA_ERR_SHAPE;
-  a.QT = pick_qt(a.nk, nq);
-  const size_t smem = static_cast<size_t>(a.QT) * a.nk * 4 +
-                      std::max(static_cast<size_t>(kMaxD) * (a.QT + kJT) * 4, static_cast<size_t>(8 * 256 * 4));
-  if (smem > 232448 - 1024) return BSA_ERR_SHAPE;
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(score_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 1024) !=
-        cudaSuccess)
-      return BSA_ERR_CUDA;
-    configured[dev] = true;
-  }
-  const int tiles = (nq + a.QT - 1) / a.QT;
-  const long long grid = static_cast<long long>(s.BH) * tiles;
-  if (grid < 1) return BSA_OK;
-  score_topk_kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(a);
+int launch_scores_only(const ScoreArgs& s, cudaStream_t stream) {
+  if (s.D % gemm::kBK || s.D <= 0 || !s.scores) return BSA_ERR_SHAPE;
+  gemm::Args a;
+  a.qp = s.qp; a.kp = s.kp; a.scores = s.scores; a.nq = s.nq; a.nk = s.nk; a.D = s.D; a.ldc = s.ldc;
+  dim3 grid((s.nk + gemm::kTile - 1) / gemm::kTile, (s.nq + gemm::kTile - 1) / gemm::kTile, s.BH);
+  if (grid.y > 65535u || grid.z > 65535u) return BSA_ERR_SHAPE;
+  gemm::score_gemm_kernel<<<grid, gemm::kThreads, 0, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
 }
-}  // namespace score
 
-int launch_score_topk(const ScoreArgs& a, cudaStream_t stream) { return score::launch(a, 1, stream); }
+int launch_topk(const float* scores, int rows, int nk, int ldc, int topk_, int32_t* idx, cudaStream_t stream) {
+  topk::Args a;
+  a.scores = scores; a.rows = rows; a.nk = nk; a.ldc = ldc; a.topk = topk_; a.idx = idx;
+  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+  if (grid == 0) return BSA_OK;
+  if (nk <= 32 * 48) topk::topk_kernel<48><<<grid, topk::kThreads, 0, stream>>>(a);
+  else if (nk <= 32 * 96) topk::topk_kernel<96><<<grid, topk::kThreads, 0, stream>>>(a);
+  else topk::topk_kernel<0><<<grid, topk::kThreads, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
+}
 
-int launch_scores_only(const ScoreArgs& a, cudaStream_t stream) { return score::launch(a, 0, stream); }
+int launch_score_topk(const ScoreArgs& s, cudaStream_t stream) {
+  int rc = launch_scores_only(s, stream);
+  if (rc) return rc;
+  return launch_topk(s.scores, s.BH * s.nq, s.nk, s.ldc, s.topk, s.idx, stream);
+}
 
 int score_device_error(int clear) {
   int v = 0;

@@ -175,11 +175,11 @@ def score_topk(qp: torch.Tensor, kp: torch.Tensor, topk: int, return_scores: boo
     if kp.shape != qp.shape:
         raise ValueError("q and k block tensors must have the same shape for top-k routing")
     idx = torch.empty((B, H, nb, topk), device=qp.device, dtype=torch.int32)
-    scores = torch.empty((B, H, nb, nb), device=qp.device, dtype=torch.float32) if return_scores else None
+    scores = torch.empty((B, H, nb, nb), device=qp.device, dtype=torch.float32)  # GEMM output, top-k input
     rc = lib().bsa_score_topk(qp.data_ptr(), kp.data_ptr(), B * H, nb, D, int(topk), idx.data_ptr(),
-                              scores.data_ptr() if scores is not None else None, _stream(qp))
+                              scores.data_ptr(), _stream(qp))
     _check(rc, "bsa_score_topk")
-    return idx, scores
+    return idx, (scores if return_scores else None)
 
 
 def topk_from_scores(score: torch.Tensor, topk: int) -> torch.Tensor:

@@ -59,5 +59,5 @@ def test_forward_scratch_size(lib):
     f = lib.bsa_forward_scratch_bytes
     f.restype = ctypes.c_int64
     f.argtypes = [ctypes.c_int] * 7
-    # 2 (Q, K) x B*H x nb x D x 4 bytes at config 2
-    assert f(1, 32, 86400, 128, 1, 1, 64) == 2 * 32 * 1350 * 128 * 4
+    # pooled Q and K (2 x B*H x nb x D fp32) + the score matrix (B*H x nb x nb rounded to 4) at config 2
+    assert f(1, 32, 86400, 128, 1, 1, 64) == 2 * 32 * 1350 * 128 * 4 + 32 * 1350 * 1352 * 4
