@@ -35,15 +35,20 @@ for _p in (REPO, PKG):
 
 METRIC = "BSA sparse TFLOP/s (4*B*H*S*k*64*D per call) at the 720p refinement shape"
 UNIT = "TFLOP/s"
+# DRAM bytes (read + write) of one attention launch per (batch, head) at the config-2 shape, from the ncu
+# capture summarised in profiles/bsa_kernels_config2_h4_full.md (423 MB for 4 heads; traffic is per head).
+ATTN_DRAM_BYTES_PER_HEAD = {"config2": (341.502976e6 + 81.440000e6) / 4}
 
 
 def _peaks():
+    """(bf16 burst TFLOP/s, bf16 sustained TFLOP/s, HBM GB/s, "measured" | "fallback")."""
     try:
         with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+        burst = float(p["bf16_tflops"])
+        return burst, float(p.get("bf16_tflops_sustained", burst)), float(p["hbm_gbs"]), "measured"
     except Exception:
-        return 1590.0, 6650.0, "fallback"
+        return 1590.0, 1400.0, 6650.0, "fallback"
 
 
 # ------------------------------------------------------------------------------- clocks
@@ -191,7 +196,7 @@ def run_ours(args, cfg):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     if cfg.H % world or cfg.S % world:
         raise SystemExit("heads and tokens must split evenly over the ranks")
-    peak_tf, peak_hbm, peak_kind = _peaks()
+    peak_tf, peak_tf_sus, peak_hbm, peak_kind = _peaks()
 
     # inputs: the full problem is generated identically on every rank; each rank keeps its
     # sequence shard (all heads, S/world tokens)
@@ -303,6 +308,8 @@ def run_ours(args, cfg):
         route_avg = statistics.mean(route_ms)
         flops_local = cfg.sparse_flops() / world
         achieved = flops_local / (attn_avg * 1e-3) / 1e12
+        per_head = ATTN_DRAM_BYTES_PER_HEAD.get(cfg.name)
+        traffic = per_head * cfg.B * (cfg.H // world) if per_head else None
         cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
@@ -323,11 +330,15 @@ def run_ours(args, cfg):
             "pct_bf16_peak": value / peak_tf,
             "kernel_ms": {"routing(pool+score+topk)": route_avg, "attention": attn_avg},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": achieved / peak_tf, "traffic": None, "peak_kind": f"{peak_kind} bf16 burst",
-                         "kernel": "bsa_attn_kernel"},
+                         "frac": achieved / peak_tf, "traffic": traffic, "peak_kind": f"{peak_kind} bf16 burst",
+                         "frac_of_sustained": achieved / peak_tf_sus, "kernel": "bsa_attn_kernel",
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 4-head capture "
+                                           "scaled per head (profiles/bsa_kernels_config2_h4_full.md)"
+                         if traffic else None},
             "e2e": {"value": cfg.sparse_flops() / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": 4 * args.steps,
+            # per step: pool Q, pool K, score GEMM, top-k, attention
+            "gpu_launches": 5 * args.steps,
             "clocks": clk.summary(),
         }
         if cpu:
