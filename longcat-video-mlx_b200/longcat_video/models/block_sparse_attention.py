@@ -99,7 +99,10 @@ def bsa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, shape: Tupl
                   return_indices: bool = False):
     """block_sparse_attention.py:201-250 (Tier A entry) on the CUDA engine.
 
-    q, k, v: [B, H, S, D] (bf16 or fp16 CUDA tensors, d contiguous), S = T*H*W, 64-token blocks.
+    q, k, v: [B, H, S, D] (bf16 or fp16, d contiguous), S = T*H*W, 64-token blocks.  CUDA tensors
+    run in place on their device.  Host (CPU) tensors are streamed through the current CUDA device
+    in head groups -- the copy in of group i+1 and the copy out of group i-1 overlap the compute of
+    group i -- and the result comes back as a host tensor (pinned), complete on return.
     rope: optional ``RotaryPositionalEmbedding`` tables from ``rope_3d.rope_tables(...)``; when
     given, q and k are pre-RoPE and the rotation is fused into the routing kernel.
     Returns [B, H, S, D] (and the [B, H, nb, k] routing when ``return_indices``).
@@ -111,5 +114,78 @@ def bsa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, shape: Tupl
     nb = S // (chunk_thw[0] * chunk_thw[1] * chunk_thw[2])
     k_sel = num_selected_blocks(nb, sparsity) if topk is None else int(topk)
     rope_arg = rope.native_args() if rope is not None else None
-    out, idx = _native.forward(q, k, v, shape, chunk_thw, k_sel, sm_scale, rope=rope_arg)
+    if not q.is_cuda and not k.is_cuda and not v.is_cuda:
+        out, idx = _forward_host_streamed(q, k, v, shape, chunk_thw, k_sel, sm_scale, rope_arg, return_indices)
+    else:
+        out, idx = _native.forward(q, k, v, shape, chunk_thw, k_sel, sm_scale, rope=rope_arg)
     return (out, idx) if return_indices else out
+
+
+def _forward_host_streamed(q, k, v, shape, chunk_thw, k_sel, sm_scale, rope_arg, want_indices,
+                           heads_per_group: Optional[int] = None):
+    """BSA call on host tensors: three-stream pipeline over head groups on the current CUDA device.
+
+    Heads are independent (routing and attention are per (b, h)), so the call splits into head
+    groups.  Group i is copied in on a copy-in stream, computed on the current stream, and copied
+    out on a copy-out stream; two device slots alternate, so the host-to-device copy of group i+1
+    and the device-to-host copy of group i-1 run while group i computes.
+    """
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("q, k, v must have the same shape [B, H, S, D]")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k, v must share one dtype")
+    if not torch.cuda.is_available():
+        raise _native.BSAError("bsa_attention on host tensors needs a CUDA device (there is no CPU path)")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B, H, S, D = (int(x) for x in q.shape)
+    nb = S // (chunk_thw[0] * chunk_thw[1] * chunk_thw[2])
+    G = heads_per_group or max(1, min(H, H // 16 if H >= 16 else 1))
+    groups = [(h0, min(h0 + G, H)) for h0 in range(0, H, G)]
+    out = torch.empty((B, H, S, D), dtype=q.dtype, pin_memory=True)
+    idx_host = torch.empty((B, H, nb, k_sel), dtype=torch.int32, pin_memory=True) if want_indices else None
+    compute = torch.cuda.current_stream(dev)
+    s_in = torch.cuda.Stream(dev)
+    s_out = torch.cuda.Stream(dev)
+    nslot = min(2, len(groups))
+    # flat slot buffers; a group of n heads uses a contiguous [B, n, ...] view of the front
+    qd, kd, vd, od = ([torch.empty((B * G * S * D,), device=dev, dtype=q.dtype) for _ in range(nslot)]
+                      for _ in range(4))
+    idd = [torch.empty((B * G * nb * k_sel,), device=dev, dtype=torch.int32) for _ in range(nslot)]
+
+    def view(buf, n, *rest):
+        m = B * n
+        for r in rest:
+            m *= r
+        return buf[:m].view(B, n, *rest)
+
+    nbytes = int(_native.lib().bsa_forward_scratch_bytes(B, G, S, D, *chunk_thw))
+    scratch = torch.empty((max(nbytes, 16),), device=dev, dtype=torch.uint8)
+    ev_in = [torch.cuda.Event() for _ in groups]
+    ev_done = [torch.cuda.Event() for _ in groups]
+    ev_out = [torch.cuda.Event() for _ in groups]
+    s_in.wait_stream(compute)  # device buffers were allocated on the compute stream
+    for i, (h0, h1) in enumerate(groups):
+        n, sl = h1 - h0, i % nslot
+        with torch.cuda.stream(s_in):
+            if i >= nslot:
+                s_in.wait_event(ev_done[i - nslot])  # slot inputs free once group i-2 has computed
+            for dst, src in ((qd[sl], q), (kd[sl], k), (vd[sl], v)):
+                view(dst, n, S, D).copy_(src[:, h0:h1], non_blocking=True)
+            ev_in[i].record(s_in)
+        compute.wait_event(ev_in[i])
+        if i >= nslot:
+            compute.wait_event(ev_out[i - nslot])  # slot output free once group i-2 is copied out
+        _native.forward(view(qd[sl], n, S, D), view(kd[sl], n, S, D), view(vd[sl], n, S, D), shape, chunk_thw,
+                        k_sel, sm_scale, rope=rope_arg, out=view(od[sl], n, S, D),
+                        block_indices=view(idd[sl], n, nb, k_sel), scratch=scratch)
+        ev_done[i].record(compute)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_done[i])
+            out[:, h0:h1].copy_(view(od[sl], n, S, D), non_blocking=True)
+            if idx_host is not None:
+                idx_host[:, h0:h1].copy_(view(idd[sl], n, nb, k_sel), non_blocking=True)
+            ev_out[i].record(s_out)
+    compute.wait_stream(s_out)
+    compute.wait_stream(s_in)
+    ev_out[-1].synchronize()
+    return out, idx_host

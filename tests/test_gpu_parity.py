@@ -329,3 +329,25 @@ def test_attention_hook_routes_to_engine(cuda):
     attn.bsa_sparsity = 0.75
     part = attn(x, (8, 8, 8))
     assert torch.isfinite(part).all()
+
+
+@pytest.mark.parametrize("B,H,group", [(1, 5, 2), (2, 3, None), (1, 32, None)])
+def test_host_tensors_stream_through_gpu(cuda, B, H, group):
+    """Host q/k/v: the head-group pipeline returns a host tensor equal bit for bit to the device call
+    (heads are independent; the same kernels run on the same values), ragged last group included."""
+    from longcat_video.models import block_sparse_attention as bsa
+
+    S = 1024 if H < 32 else 4096
+    q, k, v = (_rand((B, H, S, 128), torch.bfloat16, s, "cpu") for s in (90, 91, 92))
+    shape, chunk, topk = (1, 1, S), (1, 1, 64), 3
+    dev_out, dev_idx = bsa.bsa_attention(q.to(cuda), k.to(cuda), v.to(cuda), shape, chunk_thw=chunk, topk=topk,
+                                         return_indices=True)
+    if group is None:
+        host_out, host_idx = bsa.bsa_attention(q.pin_memory(), k.pin_memory(), v.pin_memory(), shape,
+                                               chunk_thw=chunk, topk=topk, return_indices=True)
+    else:
+        host_out, host_idx = bsa._forward_host_streamed(q, k, v, shape, chunk, topk, 1.0 / math.sqrt(128), None,
+                                                        True, heads_per_group=group)
+    assert host_out.device.type == "cpu" and host_idx.device.type == "cpu"
+    assert torch.equal(host_idx, dev_idx.cpu())
+    assert torch.equal(host_out, dev_out.cpu())

@@ -141,3 +141,57 @@ def test_ulysses_resharding_gloo_world2():
     for p in procs:
         p.join(timeout=60)
     assert res == {0: True, 1: True}
+
+
+def _fake_bsa(q, k, v, shape, sparsity=0.9375, chunk_thw=(4, 4, 4), sm_scale=None, *, topk=None, rope=None):
+    """CPU stand-in for the engine call with the dependencies BSA has: every output token of a head
+    needs the whole sequence of that head (reversed k, per-head mean of v)."""
+    return q + 10 * k.flip(-2) + 100 * v.mean(dim=-2, keepdim=True)
+
+
+def _ulysses_pipeline_worker(rank, world, port, q, groups):
+    import torch.distributed as dist
+
+    import longcat_video.context_parallel as cp
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cp.bsa_attention = _fake_bsa
+        B, H, S, D = 2, 8, 12, 3
+        g = torch.Generator().manual_seed(5)
+        fq, fk, fv = (torch.randn((B, H, S, D), generator=g) for _ in range(3))
+        want = _fake_bsa(fq, fk, fv, (1, 1, S))
+        Sl = S // world
+        sh = slice(rank * Sl, (rank + 1) * Sl)
+        got = cp.ulysses_bsa_attention(fq[:, :, sh].contiguous(), fk[:, :, sh].contiguous(),
+                                       fv[:, :, sh].contiguous(), (1, 1, S), head_groups=groups)
+        q.put((rank, bool(torch.allclose(got, want[:, :, sh], atol=1e-5))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("groups", [1, 2, 4, 3])
+def test_ulysses_head_group_pipeline_gloo_world2(groups):
+    """The head-group pipelined exchange (async all-to-alls around each group's call) returns the
+    same sequence shards as the unsharded call, for any group count (3 falls back to 2)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ulysses_pipeline_worker, args=(r, 2, port, q, groups)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}
+
+
+def test_head_group_choice():
+    from longcat_video.context_parallel import _head_groups
+
+    assert _head_groups(32, 2, None) == 4 and _head_groups(32, 8, None) == 4
+    assert _head_groups(8, 8, None) == 1
+    assert _head_groups(32, 8, 3) == 2  # 32/3 does not split; 2 groups of 16 heads do
+    assert _head_groups(24, 8, 2) == 1  # 12 heads per group do not split over 8 ranks
