@@ -97,7 +97,7 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
 }
 
 // 5-D tiled TMA load into this CTA's shared memory, completion counted in
-// bytes on `bar`.  No multicast: the kernels here also run in multi-GPU jobs.
+// bytes on `bar`.  Plain per-CTA loads only: the kernels here also run in multi-GPU jobs.
 __device__ __forceinline__ void tma_load_5d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
                                             int c1, int c2, int c3, int c4) {
   asm volatile(
