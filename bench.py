@@ -234,7 +234,9 @@ def run_ours(args, cfg):
     def step(i=None):
         if world > 1:
             # sequence shards in, sequence shards out: head-group pipelined all-to-all around the call
-            return ulysses_bsa_attention(q, k, v, cfg.shape, chunk_thw=cfg.chunk, topk=cfg.topk, rope=rope)
+            return ulysses_bsa_attention(q, k, v, cfg.shape, chunk_thw=cfg.chunk, topk=cfg.topk, rope=rope,
+                                         sm_reserve=args.sm_reserve, head_groups=args.head_groups,
+                                         exchange=args.exchange)
         return local_call(q, k, v, i)
 
     for _ in range(args.warmup):
@@ -285,7 +287,9 @@ def run_ours(args, cfg):
     def e2e_step():
         if world > 1:
             dq, dk, dv = (h.to(dev, non_blocking=True) for h in (hq, hk, hv))
-            o = ulysses_bsa_attention(dq, dk, dv, cfg.shape, chunk_thw=cfg.chunk, topk=cfg.topk, rope=rope)
+            o = ulysses_bsa_attention(dq, dk, dv, cfg.shape, chunk_thw=cfg.chunk, topk=cfg.topk, rope=rope,
+                                      sm_reserve=args.sm_reserve, head_groups=args.head_groups,
+                                      exchange=args.exchange)
             hout.copy_(o, non_blocking=True)
         else:
             # host tensors in, host tensor out: the API streams head groups through the GPU
@@ -336,6 +340,7 @@ def run_ours(args, cfg):
             "config": {"workload": cfg.name, "B": cfg.B, "H": cfg.H, "S": S, "D": D, "topk": cfg.topk, "block": 64,
                        "blocks": "contiguous 64-token", "rope_fused": cfg.rope,
                        "parallelism": f"ulysses-heads{world}" if world > 1 else "single-gpu",
+                       "exchange": args.exchange if world > 1 else None,
                        "l2": "inputs 2.1 GB > 126 MB L2, no flush"},
             "pct_bf16_peak": value / peak_tf,
             "kernel_ms": {"routing(pool+score+topk)": route_avg, "attention": attn_avg},
@@ -354,6 +359,9 @@ def run_ours(args, cfg):
         if cpu:
             line["cpu_baseline"] = cpu
     if world > 1:
+        from longcat_video.context_parallel import close_exchanges
+
+        close_exchanges()
         dist.barrier()
         dist.destroy_process_group()
     if line is not None:
@@ -372,6 +380,12 @@ def main(argv=None):
     ap.add_argument("--ref-qblocks", type=int, default=256,
                     help="q blocks of one head in each CPU sample (bounds the CPU run time)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sm-reserve", type=int, default=None,
+                    help="N>1: SMs kept free of the attention kernel for the exchange (default: library default)")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "copy_engine", "messages"],
+                    help="N>1: all-to-all implementation (default: copy engines where they apply)")
+    ap.add_argument("--head-groups", type=int, default=None,
+                    help="N>1: head groups of the pipelined exchange (default: library default)")
     ap.add_argument("--heads", type=int, default=None,
                     help="override the head count (small cases for profiling; not a bench line)")
     args = ap.parse_args(argv)

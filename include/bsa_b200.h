@@ -108,6 +108,21 @@ int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, i
                 int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot, void* scratch,
                 int32_t* block_indices, void* out, const int64_t* out_strides, void* stream);
 
+/* The same two calls with `sm_reserve`: the persistent attention kernel then runs on (SM count -
+ * sm_reserve) CTAs (at least 1), leaving sm_reserve SMs free for kernels on other streams -- the
+ * all-to-all of a sequence-parallel job, whose kernels could not start next to an attention kernel
+ * that holds every SM.  sm_reserve = 0 is the plain call. */
+int bsa_attention_indices_ex(const void* q, const void* k, const void* v, const int32_t* block_indices, int dtype,
+                             int B, int H, int S, int D, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, int T, int Hl, int Wl, int cT, int cH, int cW, int topk,
+                             float sm_scale, void* out, const int64_t* out_strides, int sm_reserve, void* stream);
+int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl,
+                   int Wl, int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt,
+                   int rope_dh, int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot,
+                   void* scratch, int32_t* block_indices, void* out, const int64_t* out_strides, int sm_reserve,
+                   void* stream);
+
 /* bsa_forward without caller-provided scratch -- no counterpart in the reference (MLX manages
  * memory itself); it exists for callers that cannot allocate device memory where they call
  * attention (a region whose memory is fixed in advance, an embedder that owns the whole device
@@ -126,6 +141,23 @@ int bsa_forward_noalloc(const void* q, const void* k, const void* v, int dtype, 
                         int Wl, int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt,
                         int rope_dh, int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot,
                         int32_t* block_indices, void* out, const int64_t* out_strides, void* stream);
+
+/* ---- peer exchange helpers (sequence-parallel all-to-all over NVLink by the copy engines) ----
+ * No counterpart in the reference (the MLX port has no multi-GPU path; the upstream PyTorch model
+ * used NCCL all-to-all).  These are the only allocating entry points: the exchange owns a few
+ * persistent buffers per process group and shape, which other processes of the node map.
+ * bsa_ipc_alloc: cudaMalloc `bytes` and export it; `handle` receives BSA_IPC_HANDLE_BYTES bytes.
+ * bsa_ipc_open : map a buffer exported by another process of the node (peer access enabled);
+ *                bsa_ipc_close unmaps it, bsa_ipc_free frees a buffer of bsa_ipc_alloc.
+ * bsa_copy_2d  : `height` rows of `width` bytes, pitches in bytes, any mix of local and mapped peer
+ *                memory, asynchronous on `stream` (copy engine). */
+#define BSA_IPC_HANDLE_BYTES 64
+int bsa_ipc_alloc(int64_t bytes, void** ptr, unsigned char* handle);
+int bsa_ipc_free(void* ptr);
+int bsa_ipc_open(const unsigned char* handle, void** ptr);
+int bsa_ipc_close(void* ptr);
+int bsa_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                void* stream);
 
 #ifdef __cplusplus
 }

@@ -694,7 +694,9 @@ int launch_attn(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensor
   p.out_ss = a.out_ss;
   p.scale_log2 = a.sm_scale * 1.4426950408889634f;
   p.total_units = p.BH * a.nb;
-  const int grid = p.total_units < sms ? p.total_units : sms;
+  int ctas = sms - a.sm_reserve;
+  if (ctas < 1) ctas = 1;
+  const int grid = p.total_units < ctas ? p.total_units : ctas;
   if (grid <= 0) return BSA_OK;
   if (a.is_bf16)
     bsa_attn_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(*tm_q, *tm_k, *tm_v, p);

@@ -210,6 +210,15 @@ int bsa_attention_indices(const void* q, const void* k, const void* v, const int
                           int B, int H, int S, int D, const int64_t* q_strides, const int64_t* k_strides,
                           const int64_t* v_strides, int T, int Hl, int Wl, int cT, int cH, int cW, int topk,
                           float sm_scale, void* out, const int64_t* out_strides, void* stream) {
+  return bsa_attention_indices_ex(q, k, v, block_indices, dtype, B, H, S, D, q_strides, k_strides, v_strides, T, Hl,
+                                  Wl, cT, cH, cW, topk, sm_scale, out, out_strides, 0, stream);
+}
+
+int bsa_attention_indices_ex(const void* q, const void* k, const void* v, const int32_t* block_indices, int dtype,
+                             int B, int H, int S, int D, const int64_t* q_strides, const int64_t* k_strides,
+                             const int64_t* v_strides, int T, int Hl, int Wl, int cT, int cH, int cW, int topk,
+                             float sm_scale, void* out, const int64_t* out_strides, int sm_reserve, void* stream) {
+  if (sm_reserve < 0) return fail(BSA_ERR_ARG, "sm_reserve=%d must be >= 0", sm_reserve);
   if (!q || !k || !v || !block_indices || !out || !q_strides || !k_strides || !v_strides || !out_strides)
     return fail(BSA_ERR_ARG, "null pointer");
   if (dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
@@ -234,6 +243,7 @@ int bsa_attention_indices(const void* q, const void* k, const void* v, const int
   a.out_sb = out_strides[0]; a.out_sh = out_strides[1]; a.out_ss = out_strides[2];
   a.sm_scale = sm_scale;
   a.is_bf16 = dtype == BSA_DTYPE_BF16;
+  a.sm_reserve = sm_reserve;
   rc = bsa::launch_attn(&mq, &mk, &mv, a, static_cast<cudaStream_t>(stream));
   if (rc == BSA_ERR_CUDA) return cuda_fail("attention kernel launch");
   return rc;
@@ -255,6 +265,18 @@ int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, i
                 int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt, int rope_dh,
                 int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot, void* scratch,
                 int32_t* block_indices, void* out, const int64_t* out_strides, void* stream) {
+  return bsa_forward_ex(q, k, v, dtype, B, H, S, D, q_strides, k_strides, v_strides, T, Hl, Wl, cT, cH, cW, topk,
+                        sm_scale, rope, rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, q_rot, k_rot, scratch,
+                        block_indices, out, out_strides, 0, stream);
+}
+
+int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl,
+                   int Wl, int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt,
+                   int rope_dh, int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot,
+                   void* scratch, int32_t* block_indices, void* out, const int64_t* out_strides, int sm_reserve,
+                   void* stream) {
+  if (sm_reserve < 0) return fail(BSA_ERR_ARG, "sm_reserve=%d must be >= 0", sm_reserve);
   if (!scratch || !q_strides || !k_strides || !v_strides) return fail(BSA_ERR_ARG, "null pointer");
   if (!aligned16(scratch)) return fail(BSA_ERR_ALIGN, "scratch must be 16-byte aligned");
   if (dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
@@ -287,11 +309,11 @@ int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, i
   }
   if (rope) {
     const int64_t cst[3] = {static_cast<int64_t>(H) * S * D, static_cast<int64_t>(S) * D, D};
-    return bsa_attention_indices(q_rot, k_rot, v, block_indices, dtype, B, H, S, D, cst, cst, v_strides, T, Hl, Wl,
-                                 cT, cH, cW, topk, sm_scale, out, out_strides, stream);
+    return bsa_attention_indices_ex(q_rot, k_rot, v, block_indices, dtype, B, H, S, D, cst, cst, v_strides, T, Hl,
+                                    Wl, cT, cH, cW, topk, sm_scale, out, out_strides, sm_reserve, stream);
   }
-  return bsa_attention_indices(q, k, v, block_indices, dtype, B, H, S, D, q_strides, k_strides, v_strides, T, Hl,
-                               Wl, cT, cH, cW, topk, sm_scale, out, out_strides, stream);
+  return bsa_attention_indices_ex(q, k, v, block_indices, dtype, B, H, S, D, q_strides, k_strides, v_strides, T, Hl,
+                                  Wl, cT, cH, cW, topk, sm_scale, out, out_strides, sm_reserve, stream);
 }
 
 }  // extern "C"

@@ -45,6 +45,7 @@ struct AttnArgs {
   long long out_sb, out_sh, out_ss;
   float sm_scale;
   int is_bf16;
+  int sm_reserve;  // SMs left free for concurrent kernels (the persistent grid covers the rest)
 };
 int launch_attn(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, const AttnArgs& a,
                 cudaStream_t stream);

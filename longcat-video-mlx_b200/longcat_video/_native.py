@@ -51,6 +51,15 @@ _SIGNATURES = {
     "bsa_forward_scratch_bytes": ([_i, _i, _i, _i, _i, _i, _i], ctypes.c_int64),
     "bsa_forward": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i, _i, _i, _i, _f,
                      _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _c_i64p, _vp], _i),
+    "bsa_ipc_alloc": ([ctypes.c_int64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p], _i),
+    "bsa_ipc_free": ([_vp], _i),
+    "bsa_ipc_open": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)], _i),
+    "bsa_ipc_close": ([_vp], _i),
+    "bsa_copy_2d": ([_vp, ctypes.c_int64, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp], _i),
+    "bsa_attention_indices_ex": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i,
+                                  _i, _i, _i, _f, _vp, _c_i64p, _i, _vp], _i),
+    "bsa_forward_ex": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i, _i, _i, _i, _f,
+                        _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _c_i64p, _i, _vp], _i),
 }
 
 
@@ -236,8 +245,9 @@ def attention_indices(q, k, v, block_indices, shape, chunk_thw, sm_scale: float,
 
 def forward(q, k, v, shape, chunk_thw, topk: int, sm_scale: float, rope: Optional[Tuple] = None,
             out: Optional[torch.Tensor] = None, block_indices: Optional[torch.Tensor] = None,
-            scratch: Optional[torch.Tensor] = None):
-    """Full BSA call (pool -> score -> top-k -> sparse attention).  Returns (out, block_indices)."""
+            scratch: Optional[torch.Tensor] = None, sm_reserve: int = 0):
+    """Full BSA call (pool -> score -> top-k -> sparse attention).  Returns (out, block_indices).
+    ``sm_reserve`` SMs stay free of the persistent attention kernel (for a concurrent exchange)."""
     _require_cuda(q, k, v)
     if q.shape != k.shape or q.shape != v.shape:
         raise ValueError("q, k, v must have the same shape [B, H, S, D]")
@@ -260,11 +270,66 @@ def forward(q, k, v, shape, chunk_thw, topk: int, sm_scale: float, rope: Optiona
         rope_ptr = tables.data_ptr()
         q_rot = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
         k_rot = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
-    rc = lib().bsa_forward(q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype_code(q), B, H, S, D, _strides(q),
+    rc = lib().bsa_forward_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype_code(q), B, H, S, D, _strides(q),
                            _strides(k), _strides(v), T, H_, W, cT, cH, cW, int(topk), float(sm_scale), rope_ptr,
                            rdims[0], rdims[1], rdims[2], rgrid[0], rgrid[1], rgrid[2],
                            q_rot.data_ptr() if q_rot is not None else None,
                            k_rot.data_ptr() if k_rot is not None else None, scratch.data_ptr(),
-                           block_indices.data_ptr(), out.data_ptr(), _strides(out), _stream(q))
+                           block_indices.data_ptr(), out.data_ptr(), _strides(out), int(sm_reserve), _stream(q))
     _check(rc, "bsa_forward")
     return out, block_indices
+
+
+# ------------------------------------------------------------------ peer exchange helpers
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_alloc(nbytes: int) -> Tuple[int, bytes]:
+    """cudaMalloc on the current device, exported for other processes: (pointer, handle bytes)."""
+    ptr = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(lib().bsa_ipc_alloc(int(nbytes), ctypes.byref(ptr), h), "bsa_ipc_alloc")
+    return int(ptr.value), h.raw
+
+
+def ipc_free(ptr: int) -> None:
+    _check(lib().bsa_ipc_free(ptr), "bsa_ipc_free")
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map a buffer another process of the node exported; returns its address in this process."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError("IPC handle must be 64 bytes")
+    ptr = ctypes.c_void_p()
+    _check(lib().bsa_ipc_open(handle, ctypes.byref(ptr)), "bsa_ipc_open")
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(lib().bsa_ipc_close(ptr), "bsa_ipc_close")
+
+
+def copy_2d(dst: int, dpitch: int, src: int, spitch: int, width: int, height: int, stream) -> None:
+    """`height` rows of `width` bytes between any local / mapped-peer addresses, on `stream`."""
+    _check(lib().bsa_copy_2d(dst, dpitch, src, spitch, width, height, stream.cuda_stream), "bsa_copy_2d")
+
+
+class _DevBuf:
+    """__cuda_array_interface__ view of a raw device allocation (torch.as_tensor wraps it, no copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(int(x) for x in shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3, "strides": None,
+                                         "stream": None}
+
+
+def wrap_device(ptr: int, shape, dtype: torch.dtype, device) -> torch.Tensor:
+    """A torch tensor over raw device memory at `ptr` (the caller keeps the memory alive)."""
+    if dtype in (torch.bfloat16, torch.float16):
+        t = torch.as_tensor(_DevBuf(ptr, shape, "<i2"), device=device)
+        return t.view(dtype)
+    if dtype == torch.float32:
+        return torch.as_tensor(_DevBuf(ptr, shape, "<f4"), device=device)
+    if dtype == torch.int32:
+        return torch.as_tensor(_DevBuf(ptr, shape, "<i4"), device=device)
+    raise ValueError(f"unsupported dtype {dtype}")

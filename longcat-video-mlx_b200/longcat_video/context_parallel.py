@@ -21,7 +21,7 @@ import torch.distributed as dist
 
 from .models.block_sparse_attention import bsa_attention
 
-__all__ = ["seq_to_heads", "heads_to_seq", "ulysses_bsa_attention"]
+__all__ = ["seq_to_heads", "heads_to_seq", "ulysses_bsa_attention", "PeerExchange", "close_exchanges"]
 
 
 def _world(group) -> int:
@@ -65,30 +65,47 @@ def heads_to_seq(o: torch.Tensor, group=None) -> torch.Tensor:
     return recv.reshape(*lead, B, P * Hl, S // P, D)
 
 
-def _seq_to_heads_async(x: torch.Tensor, P: int, group):
-    """Start seq_to_heads of [3, B, Hg, S/P, D]; returns (work, finish) where finish() -> [3, B, Hg/P, S, D]."""
-    L, (B, H, Sl, D) = 1, x.shape[1:]
-    y = x.reshape(3, B, P, H // P, Sl, D).movedim(L + 1, 0).contiguous()
-    recv = torch.empty_like(y)
-    work = dist.all_to_all_single(recv, y, group=group, async_op=True)
+def _exchange_in(q, k, v, heads, P: int, rank: int, group):
+    """Post the exchange that gives this rank whole sequences of its heads of one head group.
 
-    def finish():
-        return recv.movedim(0, L + 2).reshape(3, B, H // P, P * Sl, D)
+    heads: the group's global head ids; rank p owns heads[p*Hl:(p+1)*Hl].  Every [S/P, D] piece
+    moves as its own point-to-point message straight from the input shard into the
+    whole-sequence buffer [3, B, Hl, S, D], so no packing copy runs on either side.  Peers post
+    their messages in the same (tensor, batch, head) order, which pairs sends with receives.
+    Returns (works, qkv_h).
+    """
+    B, _, Sl, D = q.shape
+    Hl = len(heads) // P
+    qkv_h = torch.empty((3, B, Hl, P * Sl, D), device=q.device, dtype=q.dtype)
+    ops = []
+    for t, x in enumerate((q, k, v)):
+        for b in range(B):
+            for p in range(P):
+                for j in range(Hl):
+                    if p == rank:
+                        qkv_h[t, b, j, rank * Sl:(rank + 1) * Sl].copy_(x[b, heads[rank * Hl + j]])
+                    else:
+                        ops.append(dist.P2POp(dist.isend, x[b, heads[p * Hl + j]], p, group))
+                        ops.append(dist.P2POp(dist.irecv, qkv_h[t, b, j, p * Sl:(p + 1) * Sl], p, group))
+    works = dist.batch_isend_irecv(ops) if ops else []
+    return works, qkv_h
 
-    return work, finish
 
-
-def _heads_to_seq_async(o: torch.Tensor, P: int, group):
-    """Start heads_to_seq of [B, Hg/P, S, D]; returns (work, finish) where finish() -> [B, Hg, S/P, D]."""
+def _exchange_out(o, out, heads, P: int, rank: int, group):
+    """Inverse of ``_exchange_in`` for the output: o [B, Hl, S, D] (this rank's heads, whole
+    sequence) -> out[:, heads] [B, H, S/P, D] (every head of the group, this rank's tokens)."""
     B, Hl, S, D = o.shape
-    y = o.reshape(B, Hl, P, S // P, D).movedim(2, 0).contiguous()
-    recv = torch.empty_like(y)
-    work = dist.all_to_all_single(recv, y, group=group, async_op=True)
-
-    def finish():
-        return recv.movedim(0, 1).reshape(B, P * Hl, S // P, D)
-
-    return work, finish
+    Sl = S // P
+    ops = []
+    for b in range(B):
+        for p in range(P):
+            for j in range(Hl):
+                if p == rank:
+                    out[b, heads[rank * Hl + j]].copy_(o[b, j, rank * Sl:(rank + 1) * Sl])
+                else:
+                    ops.append(dist.P2POp(dist.isend, o[b, j, p * Sl:(p + 1) * Sl], p, group))
+                    ops.append(dist.P2POp(dist.irecv, out[b, heads[p * Hl + j]], p, group))
+    return dist.batch_isend_irecv(ops) if ops else []
 
 
 def _head_groups(H: int, P: int, groups: Optional[int]) -> int:
@@ -100,41 +117,216 @@ def _head_groups(H: int, P: int, groups: Optional[int]) -> int:
     return groups
 
 
+# SMs left to the message exchange's kernels while the persistent attention kernel runs
+DEFAULT_SM_RESERVE = 8
+
+
+class PeerExchange:
+    """Copy-engine all-to-all for the sequence-parallel BSA call (one per process group and shape).
+
+    Persistent buffers, mapped by every rank of the node once (CUDA IPC):
+      stage    [3, B, H, S/P, D]  this rank's q/k/v shard, which peers read
+      out_recv [B, H, S/P, D]     this rank's output shard, which peers write
+    and local ones: two whole-sequence input slots [3, B, Hl, S, D] and two output slots
+    [B, Hl, S, D] (Hl = heads of one group owned by this rank).
+
+    One call: stage q/k/v (local copy), barrier, then per head group g a copy-in stream pulls the
+    group's pieces from every peer's stage into slot g%2 (one 2-D copy per peer, tensor and batch),
+    the compute stream runs BSA on it, and a copy-out stream pushes each peer's token range of the
+    output straight into that peer's out_recv.  A final barrier (after this rank's last push)
+    means every peer's pushes into this rank's out_recv are complete.  Copy engines carry every
+    transfer over NVLink, so the attention kernel keeps all SMs.  Two barriers per call (a 4-byte
+    all-reduce each); no host synchronisation.
+    """
+
+    def __init__(self, B: int, H: int, Sl: int, D: int, dtype: torch.dtype, groups: int, group, device):
+        from . import _native
+
+        self.P = _world(group)
+        self.rank = dist.get_rank(group)
+        self.group = group
+        self.device = device
+        self.B, self.H, self.Sl, self.D, self.dtype, self.G = B, H, Sl, D, dtype, groups
+        self.Hg = H // groups
+        self.Hl = self.Hg // self.P
+        self.S = Sl * self.P
+        self.elt = torch.empty((), dtype=dtype).element_size()
+        with torch.cuda.device(device):
+            stage_ptr, h_stage = _native.ipc_alloc(3 * B * H * Sl * D * self.elt)
+            outr_ptr, h_outr = _native.ipc_alloc(B * H * Sl * D * self.elt)
+        self._own = [stage_ptr, outr_ptr]
+        handles = [None] * self.P
+        dist.all_gather_object(handles, (h_stage, h_outr), group=group)
+        self._opened = []
+        self.peer_stage, self.peer_outr = [], []
+        with torch.cuda.device(device):
+            for p in range(self.P):
+                if p == self.rank:
+                    self.peer_stage.append(stage_ptr)
+                    self.peer_outr.append(outr_ptr)
+                else:
+                    a, b = _native.ipc_open(handles[p][0]), _native.ipc_open(handles[p][1])
+                    self._opened += [a, b]
+                    self.peer_stage.append(a)
+                    self.peer_outr.append(b)
+        self.stage = _native.wrap_device(stage_ptr, (3, B, H, Sl, D), dtype, device)
+        self.out_recv = _native.wrap_device(outr_ptr, (B, H, Sl, D), dtype, device)
+        self.recv_in = [torch.empty((3, B, self.Hl, self.S, D), device=device, dtype=dtype) for _ in range(2)]
+        self.o_slot = [torch.empty((B, self.Hl, self.S, D), device=device, dtype=dtype) for _ in range(2)]
+        self.flag = torch.zeros((1,), device=device, dtype=torch.int32)
+        self.s_in = torch.cuda.Stream(device)
+        self.s_out = torch.cuda.Stream(device)
+        self._native = _native
+
+    def _barrier(self):
+        dist.all_reduce(self.flag, group=self.group)  # on the current stream; no host wait
+
+    def run(self, q, k, v, compute) -> torch.Tensor:
+        """q, k, v: [B, H, S/P, D] shards; compute(qh, kh, vh, out) runs BSA on one group's
+        whole-sequence heads [B, Hl, S, D] into out.  Returns the output shard [B, H, S/P, D]."""
+        nat, P, r = self._native, self.P, self.rank
+        B, H, Sl, D, S, Hl, Hg, e = self.B, self.H, self.Sl, self.D, self.S, self.Hl, self.Hg, self.elt
+        C = torch.cuda.current_stream(self.device)
+        for t, x in enumerate((q, k, v)):
+            self.stage[t].copy_(x)
+        self._barrier()  # every rank has staged this call's inputs and finished its previous call
+        ev_start = torch.cuda.Event()
+        ev_start.record(C)
+        self.s_in.wait_event(ev_start)
+        ev_comp, ev_push = [], []
+        piece, row = Sl * D * e, S * D * e
+        for g in range(self.G):
+            sl = g % 2
+            h0 = g * Hg + r * Hl  # first head of this group that this rank computes
+            if g >= 2:
+                self.s_in.wait_event(ev_comp[g - 2])  # input slot free
+            dst0 = self.recv_in[sl].data_ptr()
+            for p in range(P):
+                for t in range(3):
+                    for b in range(B):
+                        src = self.peer_stage[p] + ((t * B + b) * H + h0) * piece
+                        dst = dst0 + ((t * B + b) * Hl * S + p * Sl) * D * e
+                        nat.copy_2d(dst, row, src, piece, piece, Hl, self.s_in)
+            ev_in = torch.cuda.Event()
+            ev_in.record(self.s_in)
+            C.wait_event(ev_in)
+            if g >= 2:
+                C.wait_event(ev_push[g - 2])  # output slot free
+            xin, o = self.recv_in[sl], self.o_slot[sl]
+            compute(xin[0], xin[1], xin[2], o)
+            ec = torch.cuda.Event()
+            ec.record(C)
+            ev_comp.append(ec)
+            self.s_out.wait_event(ec)
+            src0 = o.data_ptr()
+            for p in range(P):
+                for b in range(B):
+                    src = src0 + (b * Hl * S + p * Sl) * D * e
+                    dst = self.peer_outr[p] + (b * H + h0) * piece
+                    nat.copy_2d(dst, piece, src, row, piece, Hl, self.s_out)
+            ep = torch.cuda.Event()
+            ep.record(self.s_out)
+            ev_push.append(ep)
+        C.wait_event(ev_push[-1])
+        C.wait_stream(self.s_in)
+        self._barrier()  # every peer's pushes into this rank's out_recv are complete
+        return self.out_recv.clone()
+
+    def close(self):
+        """Unmap the peers' buffers, wait until every rank has done the same, free this rank's."""
+        torch.cuda.synchronize(self.device)
+        for ptr in self._opened:
+            self._native.ipc_close(ptr)
+        self._opened = []
+        dist.barrier(group=self.group)
+        torch.cuda.synchronize(self.device)
+        for ptr in self._own:
+            self._native.ipc_free(ptr)
+        self._own = []
+
+
+_EXCHANGES = {}
+
+
+def _peer_exchange(q, groups, group) -> Optional[PeerExchange]:
+    """The cached copy-engine exchange for this call, or None where it does not apply (CPU
+    tensors, a non-NCCL group)."""
+    if not q.is_cuda or dist.get_backend(group) != "nccl":
+        return None
+    B, H, Sl, D = q.shape
+    key = (id(group), q.device.index, B, H, Sl, D, q.dtype, groups)
+    ex = _EXCHANGES.get(key)
+    if ex is None:
+        ex = PeerExchange(B, H, Sl, D, q.dtype, groups, group, q.device)
+        _EXCHANGES[key] = ex
+    return ex
+
+
+def close_exchanges() -> None:
+    """Release the copy-engine exchanges' buffers (call on every rank, before destroy_process_group)."""
+    for ex in _EXCHANGES.values():
+        ex.close()
+    _EXCHANGES.clear()
+
+
 def ulysses_bsa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, shape: Tuple[int, int, int],
                           sparsity: float = 0.9375, chunk_thw: Tuple[int, int, int] = (4, 4, 4),
                           sm_scale: Optional[float] = None, *, topk: Optional[int] = None, rope=None,
-                          group=None, head_groups: Optional[int] = None) -> torch.Tensor:
+                          group=None, head_groups: Optional[int] = None,
+                          sm_reserve: Optional[int] = None, exchange: str = "auto") -> torch.Tensor:
     """Sequence-sharded BSA: q, k, v are this rank's [B, H, S/P, D] shards; returns the output
     shard [B, H, S/P, D].  ``shape`` is the full latent (T, H, W) of the whole sequence.
 
     The heads are processed in ``head_groups`` groups (default: up to 4, each a multiple of P
-    heads) so the exchanges overlap the compute: the all-to-all that brings in group g+1 and the
-    one that returns group g-1 run on the communicator's stream while group g computes.  Every
-    rank issues the same collectives in the same order.
+    heads) so the exchanges overlap the compute.  ``exchange``:
+      "copy_engine" -- ``PeerExchange``: CUDA IPC buffers and 2-D copies on the copy engines
+                       (no SMs taken from the attention kernel); CUDA tensors on an NCCL group;
+      "messages"    -- point-to-point messages of the process group (NCCL or gloo) on the
+                       communicator's stream, with ``sm_reserve`` SMs kept free of the attention
+                       kernel for them;
+      "auto"        -- the copy engines where they apply, else messages.
+    Every rank posts the same exchanges in the same order.
     """
     P = _world(group)
     if P == 1:
         return bsa_attention(q, k, v, shape, sparsity, chunk_thw, sm_scale, topk=topk, rope=rope)
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("q, k, v must have the same shape [B, H, S/P, D]")
+    q, k, v = (x.contiguous() for x in (q, k, v))
     B, H, Sl, D = q.shape
     if H % P:
         raise ValueError(f"{H} heads do not split over {P} ranks")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("q, k, v must share one dtype")
+    rank = dist.get_rank(group)
     G = _head_groups(H, P, head_groups)
+    if exchange in ("auto", "copy_engine"):
+        ex = _peer_exchange(q, G, group)
+        if ex is None and exchange == "copy_engine":
+            raise ValueError("the copy-engine exchange needs CUDA tensors and an NCCL process group")
+        if ex is not None:
+            def compute(qh, kh, vh, o):
+                bsa_attention(qh, kh, vh, shape, sparsity, chunk_thw, sm_scale, topk=topk, rope=rope, out=o)
+
+            return ex.run(q, k, v, compute)
+    elif exchange != "messages":
+        raise ValueError(f"unknown exchange {exchange!r}")
+    reserve = DEFAULT_SM_RESERVE if sm_reserve is None else int(sm_reserve)
     Hg = H // G
-    sl = [slice(g * Hg, (g + 1) * Hg) for g in range(G)]
+    heads = [list(range(g * Hg, (g + 1) * Hg)) for g in range(G)]
     out = torch.empty_like(q)
-    pending_in = _seq_to_heads_async(torch.stack((q[:, sl[0]], k[:, sl[0]], v[:, sl[0]])), P, group)
+    pending_in = _exchange_in(q, k, v, heads[0], P, rank, group)
     pending_out = []
     for g in range(G):
-        work, finish = pending_in
-        # enqueue the next group's exchange before this group's compute so it does not wait on it
+        works, qkv_h = pending_in
+        # post the next group's exchange before this group's compute so it does not queue behind it
         if g + 1 < G:
-            pending_in = _seq_to_heads_async(torch.stack((q[:, sl[g + 1]], k[:, sl[g + 1]], v[:, sl[g + 1]])), P,
-                                             group)
-        work.wait()
-        qkv_h = finish()
-        o = bsa_attention(qkv_h[0], qkv_h[1], qkv_h[2], shape, sparsity, chunk_thw, sm_scale, topk=topk, rope=rope)
-        pending_out.append((g, _heads_to_seq_async(o, P, group)))
-    for g, (work, finish) in pending_out:
-        work.wait()
-        out[:, sl[g]] = finish()
+            pending_in = _exchange_in(q, k, v, heads[g + 1], P, rank, group)
+        for w in works:
+            w.wait()
+        o = bsa_attention(qkv_h[0], qkv_h[1], qkv_h[2], shape, sparsity, chunk_thw, sm_scale, topk=topk, rope=rope,
+                          sm_reserve=reserve if q.is_cuda else 0)
+        pending_out.extend(_exchange_out(o, out, heads[g], P, rank, group))
+    for w in pending_out:
+        w.wait()
     return out

@@ -13,8 +13,10 @@ Differences from the MLX Tier A, all deliberate:
     selected KV blocks directly, which is the same function (the -1e9 additive mask zeroes
     exactly the unselected weights);
   * keyword-only extras: ``topk`` overrides the floor rule of :127 (the benchmark configs use
-    ceil), ``rope`` fuses the 3-D RoPE of rope_3d.py into the routing kernel, and
-    ``return_indices`` also returns the routing.
+    ceil), ``rope`` fuses the 3-D RoPE of rope_3d.py into the routing kernel,
+    ``return_indices`` also returns the routing, and ``sm_reserve`` leaves SMs free for a
+    concurrent exchange;
+  * host (CPU) tensors are streamed through the current CUDA device in head groups.
 """
 
 from __future__ import annotations
@@ -96,7 +98,7 @@ def build_token_pair_mask(block_indices: torch.Tensor, token_block_index: torch.
 def bsa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, shape: Tuple[int, int, int],
                   sparsity: float = 0.9375, chunk_thw: Tuple[int, int, int] = (4, 4, 4),
                   sm_scale: Optional[float] = None, *, topk: Optional[int] = None, rope=None,
-                  return_indices: bool = False):
+                  return_indices: bool = False, sm_reserve: int = 0, out: Optional[torch.Tensor] = None):
     """block_sparse_attention.py:201-250 (Tier A entry) on the CUDA engine.
 
     q, k, v: [B, H, S, D] (bf16 or fp16, d contiguous), S = T*H*W, 64-token blocks.  CUDA tensors
@@ -105,6 +107,9 @@ def bsa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, shape: Tupl
     group i -- and the result comes back as a host tensor (pinned), complete on return.
     rope: optional ``RotaryPositionalEmbedding`` tables from ``rope_3d.rope_tables(...)``; when
     given, q and k are pre-RoPE and the rotation is fused into the routing kernel.
+    sm_reserve: SMs kept free of the persistent attention kernel, for kernels of a concurrent
+    exchange on other streams (device tensors only).
+    out: optional preallocated [B, H, S, D] output on q's device (device tensors only).
     Returns [B, H, S, D] (and the [B, H, nb, k] routing when ``return_indices``).
     """
     if sm_scale is None:
@@ -115,9 +120,12 @@ def bsa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, shape: Tupl
     k_sel = num_selected_blocks(nb, sparsity) if topk is None else int(topk)
     rope_arg = rope.native_args() if rope is not None else None
     if not q.is_cuda and not k.is_cuda and not v.is_cuda:
+        if out is not None:
+            raise ValueError("out= is for device tensors")
         out, idx = _forward_host_streamed(q, k, v, shape, chunk_thw, k_sel, sm_scale, rope_arg, return_indices)
     else:
-        out, idx = _native.forward(q, k, v, shape, chunk_thw, k_sel, sm_scale, rope=rope_arg)
+        out, idx = _native.forward(q, k, v, shape, chunk_thw, k_sel, sm_scale, rope=rope_arg, sm_reserve=sm_reserve,
+                                   out=out)
     return (out, idx) if return_indices else out
 
 

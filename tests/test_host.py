@@ -143,7 +143,8 @@ def test_ulysses_resharding_gloo_world2():
     assert res == {0: True, 1: True}
 
 
-def _fake_bsa(q, k, v, shape, sparsity=0.9375, chunk_thw=(4, 4, 4), sm_scale=None, *, topk=None, rope=None):
+def _fake_bsa(q, k, v, shape, sparsity=0.9375, chunk_thw=(4, 4, 4), sm_scale=None, *, topk=None, rope=None,
+              sm_reserve=0):
     """CPU stand-in for the engine call with the dependencies BSA has: every output token of a head
     needs the whole sequence of that head (reversed k, per-head mean of v)."""
     return q + 10 * k.flip(-2) + 100 * v.mean(dim=-2, keepdim=True)
