@@ -121,6 +121,11 @@ def _head_groups(H: int, P: int, groups: Optional[int]) -> int:
 DEFAULT_SM_RESERVE = 8
 
 
+# copy streams per direction (peers are spread over them) and compute streams (groups alternate)
+COPY_STREAMS = 1
+COMPUTE_STREAMS = 2
+
+
 class PeerExchange:
     """Copy-engine all-to-all for the sequence-parallel BSA call (one per process group and shape).
 
@@ -174,8 +179,11 @@ class PeerExchange:
         self.recv_in = [torch.empty((3, B, self.Hl, self.S, D), device=device, dtype=dtype) for _ in range(2)]
         self.o_slot = [torch.empty((B, self.Hl, self.S, D), device=device, dtype=dtype) for _ in range(2)]
         self.flag = torch.zeros((1,), device=device, dtype=torch.int32)
-        self.s_in = torch.cuda.Stream(device)
-        self.s_out = torch.cuda.Stream(device)
+        ncopy = max(1, min(COPY_STREAMS, self.P))
+        self.s_in = [torch.cuda.Stream(device) for _ in range(ncopy)]
+        self.s_out = [torch.cuda.Stream(device) for _ in range(ncopy)]
+        self.s_comp = [torch.cuda.Stream(device) for _ in range(COMPUTE_STREAMS)]
+        self.s_join = [torch.cuda.Stream(device) for _ in range(2)]
         self._native = _native
 
     def _barrier(self):
@@ -192,43 +200,67 @@ class PeerExchange:
         self._barrier()  # every rank has staged this call's inputs and finished its previous call
         ev_start = torch.cuda.Event()
         ev_start.record(C)
-        self.s_in.wait_event(ev_start)
+        for st in self.s_in + self.s_out + self.s_comp:
+            st.wait_event(ev_start)
         ev_comp, ev_push = [], []
         piece, row = Sl * D * e, S * D * e
+        nx = len(self.s_in)
         for g in range(self.G):
             sl = g % 2
             h0 = g * Hg + r * Hl  # first head of this group that this rank computes
-            if g >= 2:
-                self.s_in.wait_event(ev_comp[g - 2])  # input slot free
+            # copy-in: one stream per peer (mod the stream count) so several copy engines share the pull
+            ev_in = []
+            for i, st in enumerate(self.s_in):
+                if g >= 2:
+                    st.wait_event(ev_comp[g - 2])  # input slot free
             dst0 = self.recv_in[sl].data_ptr()
             for p in range(P):
+                st = self.s_in[(p + r) % nx]
                 for t in range(3):
                     for b in range(B):
                         src = self.peer_stage[p] + ((t * B + b) * H + h0) * piece
                         dst = dst0 + ((t * B + b) * Hl * S + p * Sl) * D * e
-                        nat.copy_2d(dst, row, src, piece, piece, Hl, self.s_in)
-            ev_in = torch.cuda.Event()
-            ev_in.record(self.s_in)
-            C.wait_event(ev_in)
+                        nat.copy_2d(dst, row, src, piece, piece, Hl, st)
+            for st in self.s_in:
+                ev = torch.cuda.Event()
+                ev.record(st)
+                ev_in.append(ev)
+            # compute (with COMPUTE_STREAMS > 1 groups alternate between streams, so one group's
+            # kernels can start on SMs that the previous group's attention tail leaves idle)
+            cs = self.s_comp[g % len(self.s_comp)]
+            for ev in ev_in:
+                cs.wait_event(ev)
             if g >= 2:
-                C.wait_event(ev_push[g - 2])  # output slot free
+                cs.wait_event(ev_push[g - 2])  # output slot free
             xin, o = self.recv_in[sl], self.o_slot[sl]
-            compute(xin[0], xin[1], xin[2], o)
+            with torch.cuda.stream(cs):
+                compute(xin[0], xin[1], xin[2], o)
             ec = torch.cuda.Event()
-            ec.record(C)
+            ec.record(cs)
             ev_comp.append(ec)
-            self.s_out.wait_event(ec)
             src0 = o.data_ptr()
+            ev_out = []
+            for st in self.s_out:
+                st.wait_event(ec)
             for p in range(P):
+                st = self.s_out[(p + r) % len(self.s_out)]
                 for b in range(B):
                     src = src0 + (b * Hl * S + p * Sl) * D * e
                     dst = self.peer_outr[p] + (b * H + h0) * piece
-                    nat.copy_2d(dst, piece, src, row, piece, Hl, self.s_out)
+                    nat.copy_2d(dst, piece, src, row, piece, Hl, st)
+            for st in self.s_out:
+                ev = torch.cuda.Event()
+                ev.record(st)
+                ev_out.append(ev)
+            # one event that covers every copy-out stream of this group
+            joint = self.s_join[g % 2]
+            for ev in ev_out:
+                joint.wait_event(ev)
             ep = torch.cuda.Event()
-            ep.record(self.s_out)
+            ep.record(joint)
             ev_push.append(ep)
-        C.wait_event(ev_push[-1])
-        C.wait_stream(self.s_in)
+        for st in self.s_in + self.s_out + self.s_comp + self.s_join:
+            C.wait_stream(st)
         self._barrier()  # every peer's pushes into this rank's out_recv are complete
         return self.out_recv.clone()
 
