@@ -43,17 +43,21 @@ constexpr int kDP = 128;                            // head dim in shared memory
 #define BSA_KSTAGES 3
 #endif
 #ifndef BSA_VSLOTS
-#define BSA_VSLOTS 5
+#define BSA_VSLOTS 4
+#endif
+#ifndef BSA_QBUFS
+#define BSA_QBUFS 2
 #endif
 constexpr int kKStages = BSA_KSTAGES;               // K pairs
+constexpr int kQBufs = BSA_QBUFS;                   // Q tiles (2: the next unit's Q loads early)
 constexpr int kVSlots = BSA_VSLOTS;                 // V single blocks
 constexpr int kQBytes = kBlock * kDP * 2;           // 16 KB
-constexpr int kPBytes = 2 * kBlock * 64 * 2;        // 16 KB: P^T [128 kv][64 q]
+constexpr int kPBytes = 2 * kBlock * 64 * 2;        // 16 KB: P^T [128 kv][64 q] (two buffers)
 constexpr int kPairBytes = 2 * kBlock * kDP * 2;    // 32 KB: K of a block pair
 constexpr int kVBlockBytes = kBlock * kDP * 2;      // 16 KB: V of one block
 constexpr int kOffQ = 0;
-constexpr int kOffP = kOffQ + 2 * kQBytes;
-constexpr int kOffK = kOffP + kPBytes;
+constexpr int kOffP = kOffQ + kQBufs * kQBytes;
+constexpr int kOffK = kOffP + 2 * kPBytes;
 constexpr int kOffV = kOffK + kKStages * kPairBytes;
 constexpr int kTileBytes = kOffV + kVSlots * kVBlockBytes;
 #ifndef BSA_GROUP_COLS
@@ -79,8 +83,8 @@ struct SmallSmem {
   uint64_t v_empty[kVSlots];
   uint64_t s_full[2];     // QK issuer -> softmax: S^T ready
   uint64_t s_empty[2];    // softmax -> QK issuer: S^T read (256 arrivals)
-  uint64_t p_full;        // softmax -> PV issuer: P^T written (256 arrivals)
-  uint64_t p_empty;       // PV issuer -> softmax: PV done (P free, O^T up to date)
+  uint64_t p_full[2];     // softmax -> PV issuer: P^T of step g written into buffer g%2
+  uint64_t p_empty[2];    // PV issuer -> softmax: PV of step g done (buffer g%2 free, O^T up to date)
   uint64_t q_full[2];
   uint64_t q_empty[2];
   uint64_t o_empty;       // softmax -> PV issuer: O^T read by the epilogue (256 arrivals)
@@ -239,8 +243,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ss.q_empty[i], 1);
       mbar_init(&ss.drain[i], 1);
     }
-    mbar_init(&ss.p_full, kSoftmaxThreads);
-    mbar_init(&ss.p_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ss.p_full[i], kSoftmaxThreads);
+      mbar_init(&ss.p_empty[i], 1);
+    }
     mbar_init(&ss.o_empty, kSoftmaxThreads);
     ss.abort_flag = 0;
     fence_mbar_init();
@@ -278,8 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int32_t* idx = p.idx + (static_cast<long long>(bh) * p.nqb + qblk) * k;
         int nb0, nb1;
         step_blocks(idx, 0, k, p.nqb, err, nb0, nb1);
-        const int qb = n & 1;
-        if (n >= 2) ok = mbar_wait(&ss.q_empty[qb], ((n - 2) >> 1) & 1, abort_flag, err, 101, PACC(0));
+        const int qb = n % kQBufs;
+        if (n >= kQBufs) ok = mbar_wait(&ss.q_empty[qb], ((n - kQBufs) / kQBufs) & 1, abort_flag, err, 101, PACC(0));
         if (!ok) break;
         {
           int t0, h0, w0;
@@ -363,14 +369,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       int n = 0;
       bool ok = true;
       for (int unit = blockIdx.x; unit < p.total_units && ok; unit += G, ++n) {
-        const int qb = n & 1;
+        const int qb = n % kQBufs;
+        const uint32_t qpar = static_cast<uint32_t>((n / kQBufs) & 1);
         for (int j = 0; j < nsteps && ok; ++j, ++g) {
           const int ks = static_cast<int>(g % kKStages);
           const int sb = static_cast<int>(g & 1);
           ok = mbar_wait(&ss.k_full[ks], static_cast<uint32_t>((g / kKStages) & 1), abort_flag, err, 113, PACC(0));
 #ifdef BSA_MEMONLY
           // measurement build: consume K/Q without math to time the load pipeline alone
-          if (ok && j == 0) ok = mbar_wait(&ss.q_full[qb], static_cast<uint32_t>((n >> 1) & 1), abort_flag, err, 115, PACC(2));
+          if (ok && j == 0) ok = mbar_wait(&ss.q_full[qb], qpar, abort_flag, err, 115, PACC(2));
           if (!ok) break;
           mbar_arrive(&ss.k_empty[ks]);
           if (j == nsteps - 1) mbar_arrive(&ss.q_empty[qb]);
@@ -379,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #endif
           if (ok && g >= 2)
             ok = mbar_wait(&ss.s_empty[sb], static_cast<uint32_t>(((g >> 1) - 1) & 1), abort_flag, err, 114, PACC(1));
-          if (ok && j == 0) ok = mbar_wait(&ss.q_full[qb], static_cast<uint32_t>((n >> 1) & 1), abort_flag, err, 115, PACC(2));
+          if (ok && j == 0) ok = mbar_wait(&ss.q_full[qb], qpar, abort_flag, err, 115, PACC(2));
           if (!ok) break;
           tc_fence_after();
           const uint32_t kb = smem_u32(sK + ks * kPairBytes);
@@ -423,7 +430,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&ss.v_empty[vs1]);
           continue;
 #endif
-          if (ok) ok = mbar_wait(&ss.p_full, static_cast<uint32_t>(g & 1), abort_flag, err, 111, PACC(2));
+          const int pb = static_cast<int>(g & 1);
+          if (ok) ok = mbar_wait(&ss.p_full[pb], static_cast<uint32_t>((g >> 1) & 1), abort_flag, err, 111, PACC(2));
           if (ok && j == 0 && n >= 1) ok = mbar_wait(&ss.o_empty, static_cast<uint32_t>((n - 1) & 1), abort_flag, err, 112, PACC(3));
           if (!ok) break;
           tc_fence_after();
@@ -435,13 +443,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int half = 0; half < 2; ++half) {
               const int kk = half * 4 + i;
               const uint64_t ad = sdesc_sw128((half ? vb1 : vb0) + i * 2048, kVBlockBytes / 2, 1024);
-              const uint64_t bd = sdesc_sw128(pbase + kk * 2048, 16384, 1024);
+              const uint64_t bd = sdesc_sw128(pbase + pb * kPBytes + kk * 2048, 16384, 1024);
               umma_ss(tmem + kColO + half * 64, ad, bd, idesc, (j > 0 || i > 0) ? 1u : 0u);
             }
           }
           umma_commit(&ss.v_empty[vs0]);
           umma_commit(&ss.v_empty[vs1]);
-          umma_commit(&ss.p_empty);
+          umma_commit(&ss.p_empty[pb]);
         }
       }
       umma_commit(&ss.drain[1]);
@@ -536,7 +544,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int q = 0; q < kCols; ++q) x[q] -= ss.colv[c0 + q];
             if (need) {
               // O^T columns of this group must be rescaled: the previous step's PV must be complete
-              ok = mbar_wait(&ss.p_empty, static_cast<uint32_t>((g - 1) & 1), abort_flag, err, 122, PACC(3));
+              ok = mbar_wait(&ss.p_empty[(g - 1) & 1], static_cast<uint32_t>(((g - 1) >> 1) & 1), abort_flag, err, 122,
+                             PACC(3));
               if (!ok) break;
               tc_fence_after();
 #pragma unroll
@@ -573,19 +582,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             packed[q >> 1] = pack2<kBF16>(p0, p1);
           }
           PTS(6);
-          if (g >= 1) {  // the previous step's PV must be done reading the P buffer
-            ok = mbar_wait(&ss.p_empty, static_cast<uint32_t>((g - 1) & 1), abort_flag, err, 124, PACC(1));
+          if (g >= 2) {  // the PV of step g-2 must be done reading this P buffer
+            ok = mbar_wait(&ss.p_empty[g & 1], static_cast<uint32_t>(((g - 2) >> 1) & 1), abort_flag, err, 124,
+                           PACC(1));
             if (!ok) break;
           }
+          uint8_t* sPg = sP + (g & 1) * kPBytes;
           PTS_START();
 #pragma unroll
           for (int c = 0; c < kCols / 8; ++c) {
             const uint4 v = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-            *reinterpret_cast<uint4*>(sP + sw128_offset(static_cast<uint32_t>(t), static_cast<uint32_t>(c0 / 8 + c))) = v;
+            *reinterpret_cast<uint4*>(sPg + sw128_offset(static_cast<uint32_t>(t), static_cast<uint32_t>(c0 / 8 + c))) = v;
           }
           fence_proxy_async_smem();
           tc_fence_before();
-          mbar_arrive(&ss.p_full);
+          mbar_arrive(&ss.p_full[g & 1]);
           PTS(3);
         }
         if (!ok) break;
@@ -594,7 +605,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float lsum = transpose_reduce<false, kCols>(l_part, lane);
           if (lane < kCols) ss.red[wq][c0 + lane] = lsum;
         }
-        ok = mbar_wait(&ss.p_empty, static_cast<uint32_t>((g - 1) & 1), abort_flag, err, 123, PACC(2));
+        ok = mbar_wait(&ss.p_empty[(g - 1) & 1], static_cast<uint32_t>(((g - 1) >> 1) & 1), abort_flag, err, 123,
+                       PACC(2));
         if (!ok) break;
         tc_fence_after();
         float o[kCols];
