@@ -93,9 +93,45 @@ struct Geo {
   int rdt, rdh, rdw, rT, rH, rW;
 };
 
+// Raw 16-byte (fp16/bf16) or 32-byte (fp32) chunk of one token row, loaded ahead of use.
+template <typename T>
+struct Raw8 {
+  uint4 v[sizeof(T) == 4 ? 2 : 1];
+};
+template <typename T>
+__device__ __forceinline__ void load_raw(const T* p, Raw8<T>& r) {
+  r.v[0] = __ldg(reinterpret_cast<const uint4*>(p));
+  if (sizeof(T) == 4) r.v[sizeof(T) == 4 ? 1 : 0] = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+}
+__device__ __forceinline__ void to_float(const Raw8<__nv_bfloat16>& r, float (&v)[8]) {
+  const uint32_t w[4] = {r.v[0].x, r.v[0].y, r.v[0].z, r.v[0].w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ void to_float(const Raw8<__half>& r, float (&v)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&r.v[0]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void to_float(const Raw8<float>& r, float (&v)[8]) {
+  v[0] = __uint_as_float(r.v[0].x); v[1] = __uint_as_float(r.v[0].y);
+  v[2] = __uint_as_float(r.v[0].z); v[3] = __uint_as_float(r.v[0].w);
+  v[4] = __uint_as_float(r.v[1].x); v[5] = __uint_as_float(r.v[1].y);
+  v[6] = __uint_as_float(r.v[1].z); v[7] = __uint_as_float(r.v[1].w);
+}
+
 // One CTA iteration pools one (b, h, block).  Thread (g, c): row group g < rpp, 8-element chunk
 // c < tpr.  It holds rows g, g+rpp, ..., g+(NP-1)*rpp and folds them in registers (token strides
 // n/2 .. rpp); the remaining fold levels (strides rpp/2 .. 1) run in place in shared memory.
+// The rows of the CTA's next block are loaded while the current one folds, and each row's token
+// offset inside a block is computed once per thread (it is the same for every block).
 template <typename T, bool kRope, int NP>
 __global__ void __launch_bounds__(kThreads)
     pool_kernel(const T* __restrict__ x, T* xr, float* pooled, Geo g) {
@@ -104,33 +140,63 @@ __global__ void __launch_bounds__(kThreads)
   const int grp = tid / g.tpr;
   const int c = tid - grp * g.tpr;
   const bool active = grp < g.rpp;
-  const long long total = static_cast<long long>(g.B) * g.H * g.nb;
-  const int cHW = g.cH * g.cW;
+  const int total = g.B * g.H * g.nb;
   const float inv_n = 1.0f / static_cast<float>(g.n);
-  for (long long item = blockIdx.x; item < total; item += gridDim.x) {
-    const int blk = static_cast<int>(item % g.nb);
-    const long long bh = item / g.nb;
-    const int b = static_cast<int>(bh / g.H);
-    const int h = static_cast<int>(bh - static_cast<long long>(b) * g.H);
-    const int per_t = g.Bh * g.Bw;
+  // token offset of this thread's rows relative to the block's first token, (ct, ch, cw) order
+  long long roff[NP];
+  {
+    const int cHW = g.cH * g.cW;
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      const int r = grp + i * g.rpp;
+      const int ct = r / cHW;
+      const int rem = r - ct * cHW;
+      const int ch = rem / g.cW;
+      const int cw = rem - ch * g.cW;
+      roff[i] = (static_cast<long long>(ct) * g.Hl + ch) * g.Wl + cw;
+    }
+  }
+  const int per_t = g.Bh * g.Bw;
+  // first token of block `blk` and the (b, h) base pointer of `item`
+  auto locate = [&](int item, int& b, int& h, int& blk, long long& tok0) {
+    blk = item % g.nb;
+    const int bh = item / g.nb;
+    b = bh / g.H;
+    h = bh - b * g.H;
     const int bt = blk / per_t;
     const int rr = blk - bt * per_t;
     const int bhh = rr / g.Bw;
     const int bw = rr - bhh * g.Bw;
-    const int t0 = bt * g.cT, h0 = bhh * g.cH, w0 = bw * g.cW;
+    tok0 = (static_cast<long long>(bt * g.cT) * g.Hl + bhh * g.cH) * g.Wl + bw * g.cW;
+  };
+  Raw8<T> cur[NP];
+  int item = blockIdx.x;
+  if (item < total && active) {
+    int b, h, blk;
+    long long tok0;
+    locate(item, b, h, blk, tok0);
+#pragma unroll
+    for (int i = 0; i < NP; ++i) load_raw(x + b * g.sb + h * g.sh + (tok0 + roff[i]) * g.ss + c * 8, cur[i]);
+  }
+  for (; item < total; item += gridDim.x) {
+    int b, h, blk;
+    long long tok0;
+    locate(item, b, h, blk, tok0);
+    const int bh = b * g.H + h;
+    Raw8<T> nxt[NP];
+    const int next = item + gridDim.x;
+    if (next < total && active) {
+      int nb_, nh, nblk;
+      long long ntok0;
+      locate(next, nb_, nh, nblk, ntok0);
+#pragma unroll
+      for (int i = 0; i < NP; ++i)
+        load_raw(x + nb_ * g.sb + nh * g.sh + (ntok0 + roff[i]) * g.ss + c * 8, nxt[i]);
+    }
     if (active) {
       float acc[NP][8];
-      long long toks[NP];
 #pragma unroll
-      for (int i = 0; i < NP; ++i) {
-        const int r = grp + i * g.rpp;  // row inside the block, (ct, ch, cw) order
-        const int ct = r / cHW;
-        const int rem = r - ct * cHW;
-        const int ch = rem / g.cW;
-        const int cw = rem - ch * g.cW;
-        toks[i] = (static_cast<long long>(t0 + ct) * g.Hl + (h0 + ch)) * g.Wl + (w0 + cw);
-        load8(x + b * g.sb + h * g.sh + toks[i] * g.ss + c * 8, acc[i]);
-      }
+      for (int i = 0; i < NP; ++i) to_float(cur[i], acc[i]);
       if (kRope) {
         const int ht = g.rdt >> 1, hh2 = g.rdh >> 1, hw2 = g.rdw >> 1;
         const float* tab_t = g.rope;
@@ -140,7 +206,7 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int i = 0; i < NP; ++i) {
           // token position on the RoPE grid (t-major flat order, same as the attention layout)
-          const long long tok = toks[i];
+          const long long tok = tok0 + roff[i];
           const int pt = static_cast<int>(tok / rhw);
           const int prem = static_cast<int>(tok - static_cast<long long>(pt) * rhw);
           const int ph = prem / g.rW;
@@ -169,7 +235,7 @@ __global__ void __launch_bounds__(kThreads)
           }
 #pragma unroll
           for (int e = 0; e < 8; ++e) acc[i][e] = round_to(acc[i][e], x);
-          store8(xr + ((static_cast<long long>(b) * g.H + h) * g.S + tok) * g.D + c * 8, acc[i]);
+          store8(xr + (static_cast<long long>(bh) * g.S + tok) * g.D + c * 8, acc[i]);
         }
       }
       // register fold levels: rows i and i + half (token strides n/2 .. rpp)
@@ -189,8 +255,10 @@ __global__ void __launch_bounds__(kThreads)
       for (int e = tid; e < half * g.D; e += kThreads) part[e] = __fadd_rn(part[e], part[e + half * g.D]);
       __syncthreads();
     }
-    if (tid < g.D) pooled[(bh * g.nb + blk) * g.D + tid] = __fmul_rn(part[tid], inv_n);
+    if (tid < g.D) pooled[(static_cast<long long>(bh) * g.nb + blk) * g.D + tid] = __fmul_rn(part[tid], inv_n);
     __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NP; ++i) cur[i] = nxt[i];
   }
 }
 }  // namespace pool
