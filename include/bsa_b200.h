@@ -54,8 +54,8 @@ int bsa_device_error(int clear);
 
 /* mean_pool_blocks_3d -- longcat_video/models/block_sparse_attention.py:67-104.
  * pooled[bh, blk, d] = mean over the block's tokens of x[b, h, token, d], in fp32 with a fixed
- * fold-halves summation order (x[r] + x[r + n/2], recursively), n = cT*cH*cW (a power of two,
- * at most 64).  With rope != NULL the 3-D RoPE of longcat_video/models/rope_3d.py:107-128 is
+ * summation order: a pairwise tree over the block's rows in token order ((r0 + r1) + (r2 + r3)) + ...,
+ * then * 1/n; n = cT*cH*cW (a power of two, at most 64).  With rope != NULL the 3-D RoPE of longcat_video/models/rope_3d.py:107-128 is
  * applied first (fp32, rounded back to the input dtype, written to x_rot, contiguous
  * [B,H,S,D]) and the rotated values are pooled.  rope holds per-axis tables, one angle per
  * rotated pair, over the RoPE grid (rope_T, rope_H, rope_W) (token s at t = s / (H*W),

@@ -8,7 +8,8 @@
 //
 // Both orders of fp32 arithmetic are fixed so that the CPU oracle (oracle/bsa_oracle.c) can
 // reproduce every pooled value and score bit for bit:
-//   pooling : fold-halves over the n tokens of a block: x[r] + x[r + n/2], recursively, then * 1/n
+//   pooling : pairwise tree over the n tokens of a block in token order ((r0 + r1) + (r2 + r3)) + ...,
+//             then * 1/n
 //   score   : one fma chain per score over d = 0..D-1 (fmaf(q[d], k[d], acc), acc starting at 0)
 // The pool kernel is HBM-bound (one read of Q and K); the score kernel is FMA/shared-memory
 // bound and keeps each score row on chip for the selection.
@@ -27,238 +28,169 @@ __device__ int g_score_err;
 namespace pool {
 constexpr int kThreads = 256;
 
-template <typename T>
-struct Vec8;  // 8 elements = 16 bytes (16-bit types) or 32 bytes (fp32)
-
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[2 * i] = __uint_as_float(w[i] << 16);
-    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-  }
-}
-__device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-  const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(h[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-
 // round an fp32 value to T and back (RoPE output is stored in the input dtype and pooled from there)
 __device__ __forceinline__ float round_to(float x, const __nv_bfloat16*) { return __bfloat162float(__float2bfloat16_rn(x)); }
 __device__ __forceinline__ float round_to(float x, const __half*) { return __half2float(__float2half_rn(x)); }
 __device__ __forceinline__ float round_to(float x, const float*) { return x; }
 
-__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-    w[i] = *reinterpret_cast<const uint32_t*>(&h);
-  }
-  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
-}
-__device__ __forceinline__ void store8(__half* p, const float (&v)[8]) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-    w[i] = *reinterpret_cast<const uint32_t*>(&h);
-  }
-  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
-}
-__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
-  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
-  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
-}
-
 struct Geo {
   int B, H, S, D, nb, n;
   long long sb, sh, ss;
   int Hl, Wl, cT, cH, cW, Bh, Bw;
-  int tpr, rpp, np;            // threads per token row (D/8), rows per pass, passes (n / rpp)
   const float* rope;
   int rdt, rdh, rdw, rT, rH, rW;
 };
 
-// Raw 16-byte (fp16/bf16) or 32-byte (fp32) chunk of one token row, loaded ahead of use.
-template <typename T>
-struct Raw8 {
-  uint4 v[sizeof(T) == 4 ? 2 : 1];
-};
-template <typename T>
-__device__ __forceinline__ void load_raw(const T* p, Raw8<T>& r) {
-  r.v[0] = __ldg(reinterpret_cast<const uint4*>(p));
-  if (sizeof(T) == 4) r.v[sizeof(T) == 4 ? 1 : 0] = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+// Four consecutive d values of one token row: 8 bytes (fp16/bf16) or 16 bytes (fp32).
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  v[0] = __uint_as_float(u.x << 16);
+  v[1] = __uint_as_float(u.x & 0xffff0000u);
+  v[2] = __uint_as_float(u.y << 16);
+  v[3] = __uint_as_float(u.y & 0xffff0000u);
 }
-__device__ __forceinline__ void to_float(const Raw8<__nv_bfloat16>& r, float (&v)[8]) {
-  const uint32_t w[4] = {r.v[0].x, r.v[0].y, r.v[0].z, r.v[0].w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[2 * i] = __uint_as_float(w[i] << 16);
-    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-  }
+__device__ __forceinline__ void load4(const __half* p, float (&v)[4]) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
 }
-__device__ __forceinline__ void to_float(const Raw8<__half>& r, float (&v)[8]) {
-  const __half2* h = reinterpret_cast<const __half2*>(&r.v[0]);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(h[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
+__device__ __forceinline__ void load4(const float* p, float (&v)[4]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
 }
-__device__ __forceinline__ void to_float(const Raw8<float>& r, float (&v)[8]) {
-  v[0] = __uint_as_float(r.v[0].x); v[1] = __uint_as_float(r.v[0].y);
-  v[2] = __uint_as_float(r.v[0].z); v[3] = __uint_as_float(r.v[0].w);
-  v[4] = __uint_as_float(r.v[1].x); v[5] = __uint_as_float(r.v[1].y);
-  v[6] = __uint_as_float(r.v[1].z); v[7] = __uint_as_float(r.v[1].w);
+__device__ __forceinline__ void store4(__nv_bfloat16* p, const float (&v)[4]) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+  const __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+}
+__device__ __forceinline__ void store4(__half* p, const float (&v)[4]) {
+  const __half2 a = __floats2half2_rn(v[0], v[1]);
+  const __half2 b = __floats2half2_rn(v[2], v[3]);
+  *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+}
+__device__ __forceinline__ void store4(float* p, const float (&v)[4]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
 }
 
-// One CTA iteration pools one (b, h, block).  Thread (g, c): row group g < rpp, 8-element chunk
-// c < tpr.  It holds rows g, g+rpp, ..., g+(NP-1)*rpp and folds them in registers (token strides
-// n/2 .. rpp); the remaining fold levels (strides rpp/2 .. 1) run in place in shared memory.
-// The rows of the CTA's next block are loaded while the current one folds, and each row's token
-// offset inside a block is computed once per thread (it is the same for every block).
-template <typename T, bool kRope, int NP>
-__global__ void __launch_bounds__(kThreads)
+// One warp pools one (b, h, block) at a time; lane l holds d values 4l .. 4l+3 of every row.
+// Rows are read in token order, 8 at a time (all 8 loads in flight before the first is used), and
+// summed as a pairwise tree over adjacent rows: (r0 + r1), (r2 + r3), then ((r0+r1) + (r2+r3)), ...
+// kept as a binary counter of partial sums (level L holds the sum of the last complete run of 2^L
+// rows), so the order is fixed and needs no shared memory or barrier.  Each row's token offset
+// inside a block is the same for every block and is tabled once per CTA.
+template <typename T, bool kRope>
+__global__ void __launch_bounds__(kThreads, 4)
     pool_kernel(const T* __restrict__ x, T* xr, float* pooled, Geo g) {
-  __shared__ __align__(16) float part[64 * 128];  // [rpp][D] fold partials
+  __shared__ long long roff[64];  // token offset of row r from the block's first token, (ct, ch, cw) order
   const int tid = threadIdx.x;
-  const int grp = tid / g.tpr;
-  const int c = tid - grp * g.tpr;
-  const bool active = grp < g.rpp;
-  const int total = g.B * g.H * g.nb;
-  const float inv_n = 1.0f / static_cast<float>(g.n);
-  // token offset of this thread's rows relative to the block's first token, (ct, ch, cw) order
-  long long roff[NP];
-  {
+  if (tid < g.n) {
     const int cHW = g.cH * g.cW;
-#pragma unroll
-    for (int i = 0; i < NP; ++i) {
-      const int r = grp + i * g.rpp;
-      const int ct = r / cHW;
-      const int rem = r - ct * cHW;
-      const int ch = rem / g.cW;
-      const int cw = rem - ch * g.cW;
-      roff[i] = (static_cast<long long>(ct) * g.Hl + ch) * g.Wl + cw;
-    }
+    const int ct = tid / cHW;
+    const int rem = tid - ct * cHW;
+    const int ch = rem / g.cW;
+    const int cw = rem - ch * g.cW;
+    roff[tid] = (static_cast<long long>(ct) * g.Hl + ch) * g.Wl + cw;
   }
+  __syncthreads();
+  const int lane = tid & 31;
+  const int d0 = lane * 4;
+  const bool dact = d0 < g.D;
+  const int total = g.B * g.H * g.nb;
   const int per_t = g.Bh * g.Bw;
-  // first token of block `blk` and the (b, h) base pointer of `item`
-  auto locate = [&](int item, int& b, int& h, int& blk, long long& tok0) {
-    blk = item % g.nb;
+  const float inv_n = 1.0f / static_cast<float>(g.n);
+  const int nwarps = gridDim.x * (kThreads / 32);
+  for (int item = blockIdx.x * (kThreads / 32) + (tid >> 5); item < total; item += nwarps) {
+    const int blk = item % g.nb;
     const int bh = item / g.nb;
-    b = bh / g.H;
-    h = bh - b * g.H;
+    const int b = bh / g.H;
+    const int h = bh - b * g.H;
     const int bt = blk / per_t;
     const int rr = blk - bt * per_t;
     const int bhh = rr / g.Bw;
     const int bw = rr - bhh * g.Bw;
-    tok0 = (static_cast<long long>(bt * g.cT) * g.Hl + bhh * g.cH) * g.Wl + bw * g.cW;
-  };
-  Raw8<T> cur[NP];
-  int item = blockIdx.x;
-  if (item < total && active) {
-    int b, h, blk;
-    long long tok0;
-    locate(item, b, h, blk, tok0);
+    const long long tok0 = (static_cast<long long>(bt * g.cT) * g.Hl + bhh * g.cH) * g.Wl + bw * g.cW;
+    const T* base = x + b * g.sb + h * g.sh + d0;
+    float lvl[7][4];  // partial sums by tree level
+    float tot[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int r0 = 0; r0 < g.n; r0 += 8) {
+      float v[8][4];
 #pragma unroll
-    for (int i = 0; i < NP; ++i) load_raw(x + b * g.sb + h * g.sh + (tok0 + roff[i]) * g.ss + c * 8, cur[i]);
-  }
-  for (; item < total; item += gridDim.x) {
-    int b, h, blk;
-    long long tok0;
-    locate(item, b, h, blk, tok0);
-    const int bh = b * g.H + h;
-    Raw8<T> nxt[NP];
-    const int next = item + gridDim.x;
-    if (next < total && active) {
-      int nb_, nh, nblk;
-      long long ntok0;
-      locate(next, nb_, nh, nblk, ntok0);
+      for (int i = 0; i < 8; ++i) {
+        if (r0 + i < g.n && dact) load4(base + (tok0 + roff[r0 + i]) * g.ss, v[i]);
+        else v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.f;
+      }
 #pragma unroll
-      for (int i = 0; i < NP; ++i)
-        load_raw(x + nb_ * g.sb + nh * g.sh + (ntok0 + roff[i]) * g.ss + c * 8, nxt[i]);
-    }
-    if (active) {
-      float acc[NP][8];
-#pragma unroll
-      for (int i = 0; i < NP; ++i) to_float(cur[i], acc[i]);
-      if (kRope) {
-        const int ht = g.rdt >> 1, hh2 = g.rdh >> 1, hw2 = g.rdw >> 1;
-        const float* tab_t = g.rope;
-        const float* tab_h = tab_t + 2 * g.rT * ht;
-        const float* tab_w = tab_h + 2 * g.rH * hh2;
-        const int rhw = g.rH * g.rW;
-#pragma unroll
-        for (int i = 0; i < NP; ++i) {
+      for (int i = 0; i < 8; ++i) {
+        const int r = r0 + i;
+        if (r >= g.n) break;
+        if (kRope) {
+          const long long tok = tok0 + roff[r];
+          const int ht = g.rdt >> 1, hh2 = g.rdh >> 1, hw2 = g.rdw >> 1;
+          const float* tab_t = g.rope;
+          const float* tab_h = tab_t + 2 * g.rT * ht;
+          const float* tab_w = tab_h + 2 * g.rH * hh2;
+          const int rhw = g.rH * g.rW;
           // token position on the RoPE grid (t-major flat order, same as the attention layout)
-          const long long tok = tok0 + roff[i];
           const int pt = static_cast<int>(tok / rhw);
           const int prem = static_cast<int>(tok - static_cast<long long>(pt) * rhw);
           const int ph = prem / g.rW;
           const int pw = prem - ph * g.rW;
-          // rotate 4 pairs: (x0, x1) -> (x0*cos - x1*sin, x1*cos + x0*sin), fp32, no fma
+          if (dact) {
+            // rotate 2 pairs: (x0, x1) -> (x0*cos - x1*sin, x1*cos + x0*sin), fp32, no fma
 #pragma unroll
-          for (int pr = 0; pr < 4; ++pr) {
-            const int d = c * 8 + 2 * pr;
-            float cs, sn;
-            if (d < g.rdt) {
-              const int i2 = d >> 1;
-              cs = __ldg(tab_t + pt * ht + i2);
-              sn = __ldg(tab_t + g.rT * ht + pt * ht + i2);
-            } else if (d < g.rdt + g.rdh) {
-              const int i2 = (d - g.rdt) >> 1;
-              cs = __ldg(tab_h + ph * hh2 + i2);
-              sn = __ldg(tab_h + g.rH * hh2 + ph * hh2 + i2);
-            } else {
-              const int i2 = (d - g.rdt - g.rdh) >> 1;
-              cs = __ldg(tab_w + pw * hw2 + i2);
-              sn = __ldg(tab_w + g.rW * hw2 + pw * hw2 + i2);
+            for (int pr = 0; pr < 2; ++pr) {
+              const int d = d0 + 2 * pr;
+              float cs, sn;
+              if (d < g.rdt) {
+                const int i2 = d >> 1;
+                cs = __ldg(tab_t + pt * ht + i2);
+                sn = __ldg(tab_t + g.rT * ht + pt * ht + i2);
+              } else if (d < g.rdt + g.rdh) {
+                const int i2 = (d - g.rdt) >> 1;
+                cs = __ldg(tab_h + ph * hh2 + i2);
+                sn = __ldg(tab_h + g.rH * hh2 + ph * hh2 + i2);
+              } else {
+                const int i2 = (d - g.rdt - g.rdh) >> 1;
+                cs = __ldg(tab_w + pw * hw2 + i2);
+                sn = __ldg(tab_w + g.rW * hw2 + pw * hw2 + i2);
+              }
+              const float a = v[i][2 * pr], bb = v[i][2 * pr + 1];
+              v[i][2 * pr] = __fadd_rn(__fmul_rn(a, cs), __fmul_rn(-bb, sn));
+              v[i][2 * pr + 1] = __fadd_rn(__fmul_rn(bb, cs), __fmul_rn(a, sn));
             }
-            const float a = acc[i][2 * pr], bb = acc[i][2 * pr + 1];
-            acc[i][2 * pr] = __fadd_rn(__fmul_rn(a, cs), __fmul_rn(-bb, sn));
-            acc[i][2 * pr + 1] = __fadd_rn(__fmul_rn(bb, cs), __fmul_rn(a, sn));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[i][e] = round_to(v[i][e], x);
+            store4(xr + (static_cast<long long>(bh) * g.S + tok) * g.D + d0, v[i]);
+          }
+        }
+        // insert row r into the binary counter: merge with every complete run that ends at r
+        float c[4] = {v[i][0], v[i][1], v[i][2], v[i][3]};
+#pragma unroll
+        for (int L = 0; L < 7; ++L) {
+          if (((r >> L) & 1) == 0) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) lvl[L][e] = c[e];
+            break;
           }
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[i][e] = round_to(acc[i][e], x);
-          store8(xr + (static_cast<long long>(bh) * g.S + tok) * g.D + c * 8, acc[i]);
+          for (int e = 0; e < 4; ++e) c[e] = __fadd_rn(lvl[L][e], c[e]);
+          if (r + 1 == g.n && (1 << (L + 1)) == g.n) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) tot[e] = c[e];
+          }
         }
       }
-      // register fold levels: rows i and i + half (token strides n/2 .. rpp)
-#pragma unroll
-      for (int half = NP / 2; half >= 1; half >>= 1) {
-#pragma unroll
-        for (int i = 0; i < half; ++i)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[i][e] = __fadd_rn(acc[i][e], acc[i + half][e]);
-      }
-      *reinterpret_cast<float4*>(&part[grp * g.D + c * 8]) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
-      *reinterpret_cast<float4*>(&part[grp * g.D + c * 8 + 4]) = make_float4(acc[0][4], acc[0][5], acc[0][6], acc[0][7]);
     }
-    __syncthreads();
-    // shared-memory fold levels (strides rpp/2 .. 1), in place
-    for (int half = g.rpp >> 1; half >= 1; half >>= 1) {
-      for (int e = tid; e < half * g.D; e += kThreads) part[e] = __fadd_rn(part[e], part[e + half * g.D]);
-      __syncthreads();
-    }
-    if (tid < g.D) pooled[(static_cast<long long>(bh) * g.nb + blk) * g.D + tid] = __fmul_rn(part[tid], inv_n);
-    __syncthreads();
+    if (g.n == 1) {
 #pragma unroll
-    for (int i = 0; i < NP; ++i) cur[i] = nxt[i];
+      for (int e = 0; e < 4; ++e) tot[e] = lvl[0][e];
+    }
+    if (dact) {
+      const float out[4] = {__fmul_rn(tot[0], inv_n), __fmul_rn(tot[1], inv_n), __fmul_rn(tot[2], inv_n),
+                            __fmul_rn(tot[3], inv_n)};
+      store4(pooled + (static_cast<long long>(bh) * g.nb + blk) * g.D + d0, out);
+    }
   }
 }
 }  // namespace pool
@@ -271,42 +203,31 @@ int launch_pool(const PoolArgs& a, cudaStream_t stream) {
   g.sb = a.sb; g.sh = a.sh; g.ss = a.ss;
   g.Hl = a.Hl; g.Wl = a.Wl; g.cT = a.cT; g.cH = a.cH; g.cW = a.cW;
   g.Bh = a.Hl / a.cH; g.Bw = a.Wl / a.cW;
-  g.tpr = a.D / 8;
-  int rpp = 1;
-  while (rpp * 2 <= kThreads / g.tpr && rpp * 2 <= n) rpp *= 2;
-  g.rpp = rpp;
-  g.np = n / rpp;
   g.rope = a.rope; g.rdt = a.rope_dt; g.rdh = a.rope_dh; g.rdw = a.rope_dw;
   g.rT = a.rope_T; g.rH = a.rope_H; g.rW = a.rope_W;
-  if (g.np > 4 || g.np * g.rpp != n) return BSA_ERR_SHAPE;
+  if (n < 1 || n > 64 || (n & (n - 1)) || a.D > 128 || a.D % 4) return BSA_ERR_SHAPE;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long long total = static_cast<long long>(a.B) * a.H * g.nb;
-  long long grid = static_cast<long long>(sms) * 6;
-  if (grid > total) grid = total;
+  long long grid = static_cast<long long>(sms) * 8;
+  const long long need = (total + kThreads / 32 - 1) / (kThreads / 32);
+  if (grid > need) grid = need;
   if (grid < 1) return BSA_OK;
   dim3 gd(static_cast<unsigned>(grid), 1, 1);
   const bool rope = a.rope != nullptr;
-#define BSA_POOL_LAUNCH_NP(TT, NP)                                                                                 \
-  do {                                                                                                             \
-    if (rope)                                                                                                      \
-      pool_kernel<TT, true, NP><<<gd, kThreads, 0, stream>>>(static_cast<const TT*>(a.x), static_cast<TT*>(a.x_rot), \
-                                                             a.pooled, g);                                         \
-    else                                                                                                           \
-      pool_kernel<TT, false, NP><<<gd, kThreads, 0, stream>>>(static_cast<const TT*>(a.x), nullptr, a.pooled, g);    \
-  } while (0)
-#define BSA_POOL_LAUNCH(TT)                        \
-  do {                                             \
-    if (g.np == 1) BSA_POOL_LAUNCH_NP(TT, 1);      \
-    else if (g.np == 2) BSA_POOL_LAUNCH_NP(TT, 2); \
-    else BSA_POOL_LAUNCH_NP(TT, 4);                \
+#define BSA_POOL_LAUNCH(TT)                                                                                      \
+  do {                                                                                                           \
+    if (rope)                                                                                                    \
+      pool_kernel<TT, true><<<gd, kThreads, 0, stream>>>(static_cast<const TT*>(a.x), static_cast<TT*>(a.x_rot),   \
+                                                         a.pooled, g);                                           \
+    else                                                                                                         \
+      pool_kernel<TT, false><<<gd, kThreads, 0, stream>>>(static_cast<const TT*>(a.x), nullptr, a.pooled, g);      \
   } while (0)
   if (a.dtype == BSA_DTYPE_BF16) BSA_POOL_LAUNCH(__nv_bfloat16);
   else if (a.dtype == BSA_DTYPE_F16) BSA_POOL_LAUNCH(__half);
   else if (a.dtype == BSA_DTYPE_F32) BSA_POOL_LAUNCH(float);
   else return BSA_ERR_DTYPE;
-#undef BSA_POOL_LAUNCH_NP
 #undef BSA_POOL_LAUNCH
   return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
 }
@@ -425,7 +346,7 @@ struct Args {
 
 // PL > 0: the row lives in registers (PL keys per lane, nk <= 32*PL); PL == 0: re-read from memory
 template <int PL>
-__global__ void __launch_bounds__(kThreads) topk_kernel(Args a) {
+__global__ void __launch_bounds__(kThreads, 4) topk_kernel(Args a) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
   if (row >= a.rows) return;

@@ -11,7 +11,8 @@
  *
  * The reference leaves the fp32 summation order to MLX; the engine fixes one and this file
  * restates exactly that order so indices can be compared bit-exactly:
- *   pooling: fold-halves over the n tokens of a block (x[r] + x[r + n/2], recursively), * (1/n)
+ *   pooling: pairwise tree over the n tokens of a block in token order, ((r0 + r1) + (r2 + r3)) + ...,
+ *            then * (1/n)
  *   scores : one fma chain per score, acc = fmaf(q[d], k[d], acc) for d = 0..D-1, acc0 = 0
  */
 #include <math.h>
@@ -35,8 +36,9 @@ void oracle_pool(const float* x, int BH, int S, int D, int T, int Hl, int Wl, in
           const long tok = ((long)(bt * cT + ct) * Hl + (bhh * cH + ch)) * Wl + (bw * cW + cw);
           buf[r] = x[((long)bh * S + tok) * D + d];
         }
-        for (int half = n / 2; half >= 1; half /= 2)
-          for (int r = 0; r < half; ++r) buf[r] = buf[r] + buf[r + half];
+        /* pairwise tree over adjacent rows: (r0 + r1), (r2 + r3), ... then pairs of those */
+        for (int stride = 1; stride < n; stride *= 2)
+          for (int r = 0; r + stride < n; r += 2 * stride) buf[r] = buf[r] + buf[r + stride];
         out[((long)bh * nb + blk) * D + d] = buf[0] * (1.0f / (float)n);
       }
     }

@@ -15,7 +15,7 @@ Parity pins (the reference cannot run here: it is MLX-only and MLX is not instal
 
 Precision: the reference pools and scores in the input dtype (``:104, :112``).  The
 oracle (and the engine) upcast to fp32 first, as the engine's contract defines
-correctness against an fp32 reference.  Pooling uses a fixed fold-halves summation
+correctness against an fp32 reference.  Pooling uses a fixed pairwise summation
 order and scoring a fixed fma chain (``oracle/bsa_oracle.c``) so that the engine's fp32
 pooled scores, and therefore its selected indices, can be compared bit-exactly.
 """
@@ -111,25 +111,24 @@ def from_block_major(y: np.ndarray, shape, chunk_thw) -> np.ndarray:
     return z.reshape(*lead, T * H_ * W, D)
 
 
-def _fold_halves_sum(y: np.ndarray, axis: int) -> np.ndarray:
-    """Sum along `axis` (power-of-two length) in the fixed order the engine uses:
-    repeatedly add the upper half onto the lower half (x[i] + x[i + n/2]), each add an
+def _pairwise_sum(y: np.ndarray, axis: int) -> np.ndarray:
+    """Sum along `axis` (power-of-two length) in the fixed order the engine uses: a pairwise
+    tree over adjacent elements, (x0 + x1), (x2 + x3), ... then pairs of those, each add an
     fp32 round-to-nearest operation."""
     y = np.moveaxis(np.asarray(y, dtype=np.float32), axis, 0)
     n = y.shape[0]
     if n & (n - 1):
-        raise ValueError("fold-halves order needs a power-of-two length")
+        raise ValueError("the pairwise order needs a power-of-two length")
     while n > 1:
-        h = n // 2
-        y = (y[:h] + y[h:n]).astype(np.float32)
-        n = h
+        y = (y[0::2] + y[1::2]).astype(np.float32)
+        n //= 2
     return y[0]
 
 
 # ----------------------------------------------------------------------------- Tier A pieces
 def mean_pool_blocks_3d(x, shape, chunk_thw=(4, 4, 4)) -> np.ndarray:
     """block_sparse_attention.py:67-104.  [B,H,S,D] -> fp32 [B,H,nb,D] in (bt,bh,bw) order.
-    fp32 mean with the fold-halves order; the 1/n scale is exact for n a power of two."""
+    fp32 mean with the pairwise order; the 1/n scale is exact for n a power of two."""
     x = to_f32(x)
     B, H, S, D = x.shape
     _check_shape(shape, chunk_thw, S)
@@ -137,7 +136,7 @@ def mean_pool_blocks_3d(x, shape, chunk_thw=(4, 4, 4)) -> np.ndarray:
     n = y.shape[-2]
     if n & (n - 1):
         return y.astype(np.float64).mean(axis=-2).astype(np.float32)
-    s = _fold_halves_sum(y, axis=3)
+    s = _pairwise_sum(y, axis=3)
     return (s * np.float32(1.0 / n)).astype(np.float32)
 
 
@@ -345,7 +344,9 @@ def apply_rope(x, cos: np.ndarray, sin: np.ndarray, out_dtype: str) -> np.ndarra
 def _load_lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
+        src = os.path.join(_HERE, "bsa_oracle.c")
+        if not os.path.exists(_LIB_PATH) or (os.path.exists(src) and
+                                             os.path.getmtime(src) > os.path.getmtime(_LIB_PATH)):
             build_oracle_lib()
         lib = ctypes.CDLL(_LIB_PATH)
         lib.oracle_scores.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
