@@ -234,6 +234,14 @@ def attention_indices(q, k, v, block_indices, shape, chunk_thw, sm_scale: float,
     nb = S // (cT * cH * cW)
     if bi.dim() != 4 or tuple(bi.shape[:3]) != (B, H, nb):
         raise ValueError(f"block_indices must be [B, H, {nb}, top_k], got {tuple(bi.shape)}")
+    if q.dtype == torch.float32:
+        # fp32 I/O (the reference kernels accept it): fp16 copies on the device, fp32 result
+        o16 = torch.empty((B, H, S, D), device=q.device, dtype=torch.float16)
+        _attention_ex(*(t.to(torch.float16) for t in (q, k, v)), bi, shape, chunk_thw, sm_scale, o16, 0)
+        if out is None:
+            return o16.float()
+        out.copy_(o16)
+        return out
     if out is None:
         out = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
     rc = lib().bsa_attention_indices(q.data_ptr(), k.data_ptr(), v.data_ptr(), bi.data_ptr(), _dtype_code(q), B, H, S,
@@ -241,6 +249,42 @@ def attention_indices(q, k, v, block_indices, shape, chunk_thw, sm_scale: float,
                                      float(sm_scale), out.data_ptr(), _strides(out), _stream(q))
     _check(rc, "bsa_attention_indices")
     return out
+
+
+def _forward_f32(q, k, v, shape, chunk_thw, topk, sm_scale, rope, out, block_indices, sm_reserve):
+    """fp32 inputs (the reference's config-1 dtype): routing runs on the fp32 values (pooling,
+    scores and top-k exactly as for 16-bit inputs); the sparse attention runs on fp16 copies made on
+    the device (fp16 keeps 11 significant bits, a relative error of ~5e-4 per input, well inside the
+    1e-2 output contract) and the output is returned in fp32."""
+    B, H, S, D = q.shape
+    qr, kr = q, k
+    if rope is not None:
+        qp, qr = mean_pool(q, shape, chunk_thw, rope=rope)
+        kp, kr = mean_pool(k, shape, chunk_thw, rope=rope)
+    else:
+        qp, _ = mean_pool(q, shape, chunk_thw)
+        kp, _ = mean_pool(k, shape, chunk_thw)
+    idx, _ = score_topk(qp, kp, topk)
+    if block_indices is not None:
+        block_indices.copy_(idx)
+        idx = block_indices
+    o16 = torch.empty((B, H, S, D), device=q.device, dtype=torch.float16)
+    qh, kh, vh = (t.to(torch.float16) for t in (qr, kr, v))
+    _attention_ex(qh, kh, vh, idx, shape, chunk_thw, sm_scale, o16, sm_reserve)
+    if out is None:
+        return o16.float(), idx
+    out.copy_(o16)
+    return out, idx
+
+
+def _attention_ex(q, k, v, bi, shape, chunk_thw, sm_scale, out, sm_reserve):
+    B, H, S, D = q.shape
+    T, H_, W, cT, cH, cW = _geometry(S, shape, chunk_thw)
+    rc = lib().bsa_attention_indices_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), bi.data_ptr(), _dtype_code(q), B,
+                                        H, S, D, _strides(q), _strides(k), _strides(v), T, H_, W, cT, cH, cW,
+                                        int(bi.shape[-1]), float(sm_scale), out.data_ptr(), _strides(out),
+                                        int(sm_reserve), _stream(q))
+    _check(rc, "bsa_attention_indices")
 
 
 def forward(q, k, v, shape, chunk_thw, topk: int, sm_scale: float, rope: Optional[Tuple] = None,
@@ -256,6 +300,8 @@ def forward(q, k, v, shape, chunk_thw, topk: int, sm_scale: float, rope: Optiona
     B, H, S, D = q.shape
     T, H_, W, cT, cH, cW = _geometry(S, shape, chunk_thw)
     nb = S // (cT * cH * cW)
+    if q.dtype == torch.float32:
+        return _forward_f32(q, k, v, shape, chunk_thw, topk, sm_scale, rope, out, block_indices, sm_reserve)
     if out is None:
         out = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
     if block_indices is None:

@@ -225,8 +225,8 @@ def test_rejections(cuda):
     with pytest.raises(ValueError, match="multiple of block_size"):
         bsa_attention_cuda(q, q, q, torch.zeros((1, 1, 1, 1), dtype=torch.int32, device=cuda), shape=(1, 1, 96),
                            chunk_thw=(1, 1, 64))
-    x = _rand((1, 1, 64, 128), torch.float32, 74, cuda)
-    with pytest.raises(ValueError, match="fp16 and bf16"):
+    x = _rand((1, 1, 64, 128), torch.float32, 74, cuda).double()
+    with pytest.raises(ValueError, match="dtype"):
         bsa_attention_cuda(x, x, x, torch.zeros((1, 1, 1, 1), dtype=torch.int32, device=cuda), shape=(4, 4, 4))
     y = _rand((1, 1, 64, 12), torch.bfloat16, 75, cuda)
     with pytest.raises(ValueError, match="multiple of 8"):
@@ -264,6 +264,27 @@ def test_forward_config1_bf16(cuda):
 
     q, k, v = (torch.from_numpy(a).to(cuda).to(torch.bfloat16) for a in make_config1_numpy(0))
     _full_forward_check(q, k, v, (1, 1, 4096), (1, 1, 64), 4)
+
+
+def test_forward_config1_fp32(cuda):
+    """Config 1 exactly as specified (fp32 inputs): fp32 routing equal to the oracle's, outputs within the
+    contract (the attention runs on device-side fp16 copies and returns fp32)."""
+    from longcat_video.workloads import make_config1_numpy
+
+    q, k, v = (torch.from_numpy(a).to(cuda) for a in make_config1_numpy(0))
+    _full_forward_check(q, k, v, (1, 1, 4096), (1, 1, 64), 4)
+
+
+def test_attention_indices_fp32_io(cuda):
+    from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
+
+    shape, chunk = (1, 1, 1024), (1, 1, 64)
+    q, k, v = (_rand((1, 2, 1024, 128), torch.float32, s, cuda) for s in (76, 77, 78))
+    idx = torch.from_numpy(np.random.default_rng(3).integers(0, 16, size=(1, 2, 16, 5)).astype(np.int32)).to(cuda)
+    out = bsa_attention_cuda(q, k, v, idx, chunk_thw=chunk, shape=shape)
+    assert out.dtype == torch.float32
+    ref = orc.bsa_sparse_attention(_np(q), _np(k), _np(v), idx.cpu().numpy(), shape, chunk)
+    _close(_np(out), ref)
 
 
 def test_forward_config1_golden_indices(cuda):
