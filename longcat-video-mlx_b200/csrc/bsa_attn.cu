@@ -82,12 +82,12 @@ struct SmallSmem {
   uint64_t v_full[kVSlots];
   uint64_t v_empty[kVSlots];
   uint64_t s_full[2];     // QK issuer -> softmax: S^T ready
-  uint64_t s_empty[2];    // softmax -> QK issuer: S^T read (256 arrivals)
-  uint64_t p_full[2];     // softmax -> PV issuer: P^T of step g written into buffer g%2
+  uint64_t s_empty[2];    // softmax -> QK issuer: S^T read (one arrival per softmax warp)
+  uint64_t p_full[2];     // softmax -> PV issuer: P^T of step g written into buffer g%2 (one per warp)
   uint64_t p_empty[2];    // PV issuer -> softmax: PV of step g done (buffer g%2 free, O^T up to date)
   uint64_t q_full[2];
   uint64_t q_empty[2];
-  uint64_t o_empty;       // softmax -> PV issuer: O^T read by the epilogue (256 arrivals)
+  uint64_t o_empty;       // softmax -> PV issuer: O^T read by the epilogue (one arrival per softmax warp)
   uint64_t drain[2];
   uint32_t tmem_base;
   int abort_flag;
@@ -238,16 +238,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ss.s_full[i], 1);
-      mbar_init(&ss.s_empty[i], kSoftmaxThreads);
+      mbar_init(&ss.s_empty[i], kSoftmaxThreads / 32);
       mbar_init(&ss.q_full[i], 1);
       mbar_init(&ss.q_empty[i], 1);
       mbar_init(&ss.drain[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&ss.p_full[i], kSoftmaxThreads);
+      mbar_init(&ss.p_full[i], kSoftmaxThreads / 32);
       mbar_init(&ss.p_empty[i], 1);
     }
-    mbar_init(&ss.o_empty, kSoftmaxThreads);
+    mbar_init(&ss.o_empty, kSoftmaxThreads / 32);
     ss.abort_flag = 0;
     fence_mbar_init();
   }
@@ -489,6 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < nsteps && ok; ++j, ++g) {
           const int sb = static_cast<int>(g & 1);
           ok = mbar_wait(&ss.s_full[sb], static_cast<uint32_t>((g >> 1) & 1), abort_flag, err, 121, PACC(0));
+          ok = __all_sync(0xffffffffu, ok);  // leave the loop warp-uniformly
           if (!ok) break;
           PTS_START();
           tc_fence_after();
@@ -546,6 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               // O^T columns of this group must be rescaled: the previous step's PV must be complete
               ok = mbar_wait(&ss.p_empty[(g - 1) & 1], static_cast<uint32_t>(((g - 1) >> 1) & 1), abort_flag, err, 122,
                              PACC(3));
+          ok = __all_sync(0xffffffffu, ok);  // leave the loop warp-uniformly
               if (!ok) break;
               tc_fence_after();
 #pragma unroll
@@ -569,7 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar_sync(bar_id, 128);  // colv is rewritten by the next slow path
           }
           tc_fence_before();
-          mbar_arrive(&ss.s_empty[sb]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ss.s_empty[sb]);  // one arrival per warp
           PTS(5);
           // ---- probabilities, row-sum partials, P^T row into the P buffer
           uint32_t packed[kCols / 2];
@@ -585,6 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (g >= 2) {  // the PV of step g-2 must be done reading this P buffer
             ok = mbar_wait(&ss.p_empty[g & 1], static_cast<uint32_t>(((g - 2) >> 1) & 1), abort_flag, err, 124,
                            PACC(1));
+          ok = __all_sync(0xffffffffu, ok);  // leave the loop warp-uniformly
             if (!ok) break;
           }
           uint8_t* sPg = sP + (g & 1) * kPBytes;
@@ -596,7 +600,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_proxy_async_smem();
           tc_fence_before();
-          mbar_arrive(&ss.p_full[g & 1]);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ss.p_full[g & 1]);
           PTS(3);
         }
         if (!ok) break;
@@ -607,6 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ok = mbar_wait(&ss.p_empty[(g - 1) & 1], static_cast<uint32_t>(((g - 1) >> 1) & 1), abort_flag, err, 123,
                        PACC(2));
+          ok = __all_sync(0xffffffffu, ok);  // leave the loop warp-uniformly
         if (!ok) break;
         tc_fence_after();
         float o[kCols];
@@ -620,7 +626,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int q = 0; q < 16; ++q) o[c + q] = __uint_as_float(ra[q]) + __uint_as_float(rb[q]);
         }
         tc_fence_before();
-        mbar_arrive(&ss.o_empty);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ss.o_empty);
         named_bar_sync(bar_id, 128);
         if (t < kCols) {
           const int c = c0 + t;

@@ -80,7 +80,7 @@ __device__ __forceinline__ void store4(float* p, const float (&v)[4]) {
 // rows), so the order is fixed and needs no shared memory or barrier.  Each row's token offset
 // inside a block is the same for every block and is tabled once per CTA.
 template <typename T, bool kRope>
-__global__ void __launch_bounds__(kThreads, 4)
+__global__ void __launch_bounds__(kThreads, kRope ? 3 : 4)
     pool_kernel(const T* __restrict__ x, T* xr, float* pooled, Geo g) {
   __shared__ long long roff[64];  // token offset of row r from the block's first token, (ct, ch, cw) order
   const int tid = threadIdx.x;
@@ -100,6 +100,27 @@ __global__ void __launch_bounds__(kThreads, 4)
   const int per_t = g.Bh * g.Bw;
   const float inv_n = 1.0f / static_cast<float>(g.n);
   const int nwarps = gridDim.x * (kThreads / 32);
+  // RoPE: each of this lane's two pairs reads one axis table (t, h or w) at a fixed column
+  const float* rcos[2] = {nullptr, nullptr};
+  const float* rsin[2] = {nullptr, nullptr};
+  int rstride[2] = {0, 0}, rax[2] = {0, 0};
+  if (kRope) {
+    const int ht = g.rdt >> 1, hh2 = g.rdh >> 1, hw2 = g.rdw >> 1;
+    const float* tab_t = g.rope;
+    const float* tab_h = tab_t + 2 * g.rT * ht;
+    const float* tab_w = tab_h + 2 * g.rH * hh2;
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr) {
+      const int d = d0 + 2 * pr;
+      if (d < g.rdt) {
+        rax[pr] = 0; rstride[pr] = ht; rcos[pr] = tab_t + (d >> 1); rsin[pr] = rcos[pr] + g.rT * ht;
+      } else if (d < g.rdt + g.rdh) {
+        rax[pr] = 1; rstride[pr] = hh2; rcos[pr] = tab_h + ((d - g.rdt) >> 1); rsin[pr] = rcos[pr] + g.rH * hh2;
+      } else {
+        rax[pr] = 2; rstride[pr] = hw2; rcos[pr] = tab_w + ((d - g.rdt - g.rdh) >> 1); rsin[pr] = rcos[pr] + g.rW * hw2;
+      }
+    }
+  }
   for (int item = blockIdx.x * (kThreads / 32) + (tid >> 5); item < total; item += nwarps) {
     const int blk = item % g.nb;
     const int bh = item / g.nb;
@@ -111,6 +132,25 @@ __global__ void __launch_bounds__(kThreads, 4)
     const int bw = rr - bhh * g.Bw;
     const long long tok0 = (static_cast<long long>(bt * g.cT) * g.Hl + bhh * g.cH) * g.Wl + bw * g.cW;
     const T* base = x + b * g.sb + h * g.sh + d0;
+    // RoPE grid positions of rows `lane` and `lane + 32` (token s at t = s / (H*W), h = (s / W) % H,
+    // w = s % W), packed as (t) and (h << 16 | w) and handed to the other lanes by shuffle
+    int posA0 = 0, posB0 = 0, posA1 = 0, posB1 = 0;
+    if (kRope) {
+      const int rhw = g.rH * g.rW;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int r = lane + 32 * hf;
+        if (r < g.n) {
+          const long long tok = tok0 + roff[r];
+          const int pt = static_cast<int>(tok / rhw);
+          const int prem = static_cast<int>(tok - static_cast<long long>(pt) * rhw);
+          const int ph = prem / g.rW;
+          const int pw = prem - ph * g.rW;
+          if (hf == 0) { posA0 = pt; posB0 = (ph << 16) | pw; }
+          else { posA1 = pt; posB1 = (ph << 16) | pw; }
+        }
+      }
+    }
     float lvl[7][4];  // partial sums by tree level
     float tot[4] = {0.f, 0.f, 0.f, 0.f};
     for (int r0 = 0; r0 < g.n; r0 += 8) {
@@ -125,43 +165,25 @@ __global__ void __launch_bounds__(kThreads, 4)
         const int r = r0 + i;
         if (r >= g.n) break;
         if (kRope) {
-          const long long tok = tok0 + roff[r];
-          const int ht = g.rdt >> 1, hh2 = g.rdh >> 1, hw2 = g.rdw >> 1;
-          const float* tab_t = g.rope;
-          const float* tab_h = tab_t + 2 * g.rT * ht;
-          const float* tab_w = tab_h + 2 * g.rH * hh2;
-          const int rhw = g.rH * g.rW;
-          // token position on the RoPE grid (t-major flat order, same as the attention layout)
-          const int pt = static_cast<int>(tok / rhw);
-          const int prem = static_cast<int>(tok - static_cast<long long>(pt) * rhw);
-          const int ph = prem / g.rW;
-          const int pw = prem - ph * g.rW;
+          // this row's position on the RoPE grid, computed by lane r % 32 at the start of the block
+          const int src = r & 31;
+          const int pt = __shfl_sync(0xffffffffu, r < 32 ? posA0 : posA1, src);
+          const int pb = __shfl_sync(0xffffffffu, r < 32 ? posB0 : posB1, src);
+          const int pax[3] = {pt, pb >> 16, pb & 0xffff};
           if (dact) {
             // rotate 2 pairs: (x0, x1) -> (x0*cos - x1*sin, x1*cos + x0*sin), fp32, no fma
 #pragma unroll
             for (int pr = 0; pr < 2; ++pr) {
-              const int d = d0 + 2 * pr;
-              float cs, sn;
-              if (d < g.rdt) {
-                const int i2 = d >> 1;
-                cs = __ldg(tab_t + pt * ht + i2);
-                sn = __ldg(tab_t + g.rT * ht + pt * ht + i2);
-              } else if (d < g.rdt + g.rdh) {
-                const int i2 = (d - g.rdt) >> 1;
-                cs = __ldg(tab_h + ph * hh2 + i2);
-                sn = __ldg(tab_h + g.rH * hh2 + ph * hh2 + i2);
-              } else {
-                const int i2 = (d - g.rdt - g.rdh) >> 1;
-                cs = __ldg(tab_w + pw * hw2 + i2);
-                sn = __ldg(tab_w + g.rW * hw2 + pw * hw2 + i2);
-              }
+              const int pos = pax[rax[pr]];
+              const float cs = __ldg(rcos[pr] + pos * rstride[pr]);
+              const float sn = __ldg(rsin[pr] + pos * rstride[pr]);
               const float a = v[i][2 * pr], bb = v[i][2 * pr + 1];
               v[i][2 * pr] = __fadd_rn(__fmul_rn(a, cs), __fmul_rn(-bb, sn));
               v[i][2 * pr + 1] = __fadd_rn(__fmul_rn(bb, cs), __fmul_rn(a, sn));
             }
 #pragma unroll
             for (int e = 0; e < 4; ++e) v[i][e] = round_to(v[i][e], x);
-            store4(xr + (static_cast<long long>(bh) * g.S + tok) * g.D + d0, v[i]);
+            store4(xr + (static_cast<long long>(bh) * g.S + tok0 + roff[r]) * g.D + d0, v[i]);
           }
         }
         // insert row r into the binary counter: merge with every complete run that ends at r
