@@ -335,7 +335,8 @@ def run_ours(args, cfg):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16" if cfg.dtype.__repr__().endswith("bfloat16") else str(cfg.dtype).split(".")[-1],
+            "vs_baseline": None, "dtype": {"torch.bfloat16": "bf16", "torch.float16": "f16",
+                      "torch.float32": "f32 I/O and routing, f16 attention"}[str(cfg.dtype)],
             "data": "synthetic (seeded; config-2 style per-block offsets)",
             "config": {"workload": cfg.name, "B": cfg.B, "H": cfg.H, "S": S, "D": D, "topk": cfg.topk, "block": 64,
                        "blocks": "contiguous 64-token", "rope_fused": cfg.rope,
