@@ -36,8 +36,8 @@ for _p in (REPO, PKG):
 METRIC = "BSA sparse TFLOP/s (4*B*H*S*k*64*D per call) at the 720p refinement shape"
 UNIT = "TFLOP/s"
 # DRAM bytes (read + write) of one attention launch per (batch, head) at the config-2 shape, from the ncu
-# capture summarised in profiles/bsa_kernels_config2_h4_full.md (436 MB for 4 heads; traffic is per head).
-ATTN_DRAM_BYTES_PER_HEAD = {"config2": (353.367552e6 + 82.623488e6) / 4}
+# capture summarised in profiles/bsa_kernels_config2_h4_full.md (426 MB for 4 heads; traffic is per head).
+ATTN_DRAM_BYTES_PER_HEAD = {"config2": (343.021312e6 + 83.094784e6) / 4}
 
 
 def _peaks():
