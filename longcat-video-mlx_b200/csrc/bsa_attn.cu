@@ -375,15 +375,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int ks = static_cast<int>(g % kKStages);
           const int sb = static_cast<int>(g & 1);
           ok = mbar_wait(&ss.k_full[ks], static_cast<uint32_t>((g / kKStages) & 1), abort_flag, err, 113, PACC(0));
-#ifdef BSA_MEMONLY
-          // measurement build: consume K/Q without math to time the load pipeline alone
-          if (ok && j == 0) ok = mbar_wait(&ss.q_full[qb], qpar, abort_flag, err, 115, PACC(2));
-          if (!ok) break;
-          mbar_arrive(&ss.k_empty[ks]);
-          if (j == nsteps - 1) mbar_arrive(&ss.q_empty[qb]);
-          (void)sb;
-          continue;
-#endif
           if (ok && g >= 2)
             ok = mbar_wait(&ss.s_empty[sb], static_cast<uint32_t>(((g >> 1) - 1) & 1), abort_flag, err, 114, PACC(1));
           if (ok && j == 0) ok = mbar_wait(&ss.q_full[qb], qpar, abort_flag, err, 115, PACC(2));
@@ -424,12 +415,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int vs1 = static_cast<int>((gb0 + 1) % kVSlots);
           ok = mbar_wait(&ss.v_full[vs0], static_cast<uint32_t>((gb0 / kVSlots) & 1), abort_flag, err, 116, PACC(0));
           if (ok) ok = mbar_wait(&ss.v_full[vs1], static_cast<uint32_t>(((gb0 + 1) / kVSlots) & 1), abort_flag, err, 117, PACC(1));
-#ifdef BSA_MEMONLY
-          if (!ok) break;
-          mbar_arrive(&ss.v_empty[vs0]);
-          mbar_arrive(&ss.v_empty[vs1]);
-          continue;
-#endif
           const int pb = static_cast<int>(g & 1);
           if (ok) ok = mbar_wait(&ss.p_full[pb], static_cast<uint32_t>((g >> 1) & 1), abort_flag, err, 111, PACC(2));
           if (ok && j == 0 && n >= 1) ok = mbar_wait(&ss.o_empty, static_cast<uint32_t>((n - 1) & 1), abort_flag, err, 112, PACC(3));
@@ -460,10 +445,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax groups
-#ifdef BSA_MEMONLY
-    if (true) {
-    } else
-#endif
     {
       const int grp = (warp - 4) >> 2;        // group g owns query columns [g*kCols, (g+1)*kCols)
       const int wq = warp & 3;                // TMEM lane quarter
