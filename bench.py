@@ -53,47 +53,115 @@ def _peaks():
 
 # ------------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clock and throttle reasons of one GPU, polled through NVML every few milliseconds by a host thread
+    (falling back to `nvidia-smi -lms 200` when NVML is unavailable).  `mark(True/False)` brackets the timed
+    region; the summary covers only the samples taken inside it."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, interval_s: float = 0.005):
         self.gpu = gpu_index
+        self.interval = interval_s
+        self.samples = []  # (t, sm_mhz, max_mhz, reasons)
+        self.window = [None, None]
+        self._stop = threading.Event()
+        self._t = None
         self.proc = None
         self.lines = []
-        self._t = None
+        self.error = None
+        self._nv = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:
+            props = torch.cuda.get_device_properties(self.gpu)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+
+    def _sample(self):
+        nv, h = self._nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        bits = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+        try:
+            sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            r = get_reasons(h)
+            self.samples.append((time.monotonic(), float(sm), float(mx), {n for n, b in bits.items() if r & b}))
+        except Exception as e:  # keep the first error for the record
+            self.error = self.error or f"{type(e).__name__}: {e}"
+
+    def _poll(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.interval)
 
     def __enter__(self):
+        self.error = None
+        self._nv = None
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self._t = threading.Thread(target=self._read, daemon=True)
+            self._nv = self._nvml_handle()
+            self._sample()
+            if not self.samples:
+                raise RuntimeError(self.error or "NVML returned no sample")
+            self._t = threading.Thread(target=self._poll, daemon=True)
             self._t.start()
-        except Exception:
-            self.proc = None
+        except Exception as e:
+            self.error = f"{type(e).__name__}: {e}"
+            self._nv = None
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                     "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self._t = threading.Thread(target=self._read, daemon=True)
+                self._t.start()
+            except Exception:
+                self.proc = None
         return self
+
+    def mark(self, start: bool):
+        """Bracket the timed region; a reading is also taken right here (so the region has samples even if
+        the polling thread is starved of the interpreter lock)."""
+        if start:
+            self.window[0] = time.monotonic()
+        if self._nv is not None:
+            self._sample()
+        if not start:
+            self.window[1] = time.monotonic()
 
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self._stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-            if self._t:
-                self._t.join(timeout=2)
+        if self._t:
+            self._t.join(timeout=2)
 
     def summary(self):
         sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        t0, t1 = self.window
+        for t, s_, m_, r in self.samples:
+            if t0 is not None and t < t0 or t1 is not None and t > t1:
+                continue
+            sm.append(s_)
+            mx = m_
+            reasons |= r
+        for ln in self.lines:  # nvidia-smi fallback
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -102,12 +170,17 @@ class ClockSampler:
                 mx = float(parts[2])
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
+            for n, v in zip(self.NAMES, parts[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+            out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        else:
+            out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                   "sm_mhz_min": min(sm)}
+        if getattr(self, "error", None):
+            out["sampler_error"] = self.error
+        return out
 
 
 # ------------------------------------------------------------------------------- CPU sample
@@ -247,16 +320,24 @@ def run_ours(args, cfg):
     torch.cuda.synchronize()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with ClockSampler(local) as clk:
+        time.sleep(0.02)  # the sampler's first reading lands before the timed region
+        clk.mark(True)
         t_start.record(stream)
         for i in range(args.steps):
+            step_ev[i].record(stream)
             step(i)
         t_end.record(stream)
         torch.cuda.synchronize()
+        clk.mark(False)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     total_ms = t_start.elapsed_time(t_end)
+    bounds = step_ev + [t_end]
+    per_step = sorted(bounds[i].elapsed_time(bounds[i + 1]) for i in range(args.steps))
+    pct = lambda q: per_step[min(len(per_step) - 1, int(q * (len(per_step) - 1) + 0.5))]
     if world > 1:
         # kernel breakdown for the roofline: the same local call on this rank's H/P whole-sequence
         # heads, timed after (outside) the timed region
@@ -335,6 +416,7 @@ def run_ours(args, cfg):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "ms_per_step_stats": {"median": pct(0.5), "p10": pct(0.1), "p90": pct(0.9), "rank": 0},
             "vs_baseline": None, "dtype": {"torch.bfloat16": "bf16", "torch.float16": "f16",
                       "torch.float32": "f32 I/O and routing, f16 attention"}[str(cfg.dtype)],
             "data": "synthetic (seeded; config-2 style per-block offsets)",
