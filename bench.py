@@ -1,12 +1,13 @@
-"""Benchmark of the 720p refinement BSA call on B200 (BASELINE metric: BSA ms/call and sparse
+"""Benchmark of the 720p refinement BSA call on B200 (metric: BSA ms/call and sparse
 TFLOP/s = 4*B*H*S*k*64*D / t, as a fraction of bf16 tensor peak).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config config2] [--impl ours|reference]
 
-One step = one full BSA call on synthetic config inputs already resident in HBM: Q/K block
-pooling, fp32 block scores + top-k, and the sparse tcgen05 attention (4 kernel launches).  At
-N > 1 (torchrun, one rank per GPU, NCCL) every rank holds a sequence shard of Q/K/V for all 32
-heads; a step is all-to-all (sequence -> heads), the BSA call on its 32/N heads, all-to-all back.
+One step = one full BSA call on synthetic config inputs already resident in HBM: Q and K block
+pooling, the fp32 block-score GEMM, top-k and the sparse tcgen05 attention (5 kernel launches).
+At N > 1 (torchrun, one rank per GPU, NCCL) every rank holds a sequence shard of Q/K/V for all
+32 heads; a step is the sequence -> heads exchange, the BSA call on its 32/N heads and the
+exchange back, pipelined over head groups (ulysses_bsa_attention).
 The problem is fixed as N grows (strong scaling).  Inputs (2.1 GB at config 2) exceed the 126 MB
 L2, so no flush is needed between steps.
 

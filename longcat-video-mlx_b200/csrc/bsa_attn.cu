@@ -20,11 +20,14 @@
 //
 // The kernel needs every (q-block, kv-block) pair's own 32 KB of K and V from L2, so the roles
 // are decoupled so that no load waits behind an unrelated one:
-//   warp 0      : Q tiles + K pairs (3-slot ring of 32 KB pairs, a slot is freed when its QK completes)
+//   warp 0      : Q tiles (two buffers) + K pairs (3-slot ring of 32 KB pairs, a slot is freed when its
+//                 QK completes)
 //   warp 1      : QK^T MMA issuer (one thread)
-//   warp 2      : V blocks (5-slot ring of 16 KB blocks, a slot is freed when its PV completes)
+//   warp 2      : V blocks (4-slot ring of 16 KB blocks, a slot is freed when its PV completes)
 //   warp 3      : PV MMA issuer (one thread)
-//   warps 4-19  : softmax groups 0..3 -- query columns 16g..16g+15 (thread t <-> TMEM lane t)
+//   warps 4-19  : softmax groups 0..3 -- query columns 16g..16g+15 (thread t <-> TMEM lane t); P^T is
+//                 double-buffered so the softmax of step g+1 does not wait for the PV of step g, and
+//                 each softmax warp arrives once (after a warp sync) on the hand-off barriers
 // One CTA per SM, persistent over (head, q-block) units in head-major order so a head's K/V stays
 // resident in L2.  Every mbarrier wait is bounded (bsa_ptx.cuh); a timeout records an error code
 // and the CTA winds down.

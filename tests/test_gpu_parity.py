@@ -1,6 +1,6 @@
 """GPU parity of the CUDA engine against the CPU oracle (oracle/bsa_oracle.py).
 
-Contract: block indices bit-exact wherever the fp32 pooled scores are
+Contract (the engine's parity target): block indices bit-exact wherever the fp32 pooled scores are
 computed identically (the engine and the oracle use the same fixed fp32 orders, so pooled means
 and scores must match bit for bit); attention outputs within relative L2 <= 1e-2 and max-abs
 <= 2e-2 of the fp32/fp64 oracle.
