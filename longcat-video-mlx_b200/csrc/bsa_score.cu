@@ -286,11 +286,12 @@ __global__ void __launch_bounds__(kThreads, 2) score_gemm_kernel(Args a) {
   const bool qv = i0 + srow < a.nq, kv = j0 + srow < a.nk;
   const float* qsrc = qp + static_cast<long long>(i0 + srow) * a.D + 4 * sd4;
   const float* ksrc = kp + static_cast<long long>(j0 + srow) * a.D + 4 * sd4;
-  float acc[8][8];
+  // accumulators in f32x2 pairs: acc2[r][p] holds scores (r, 2p) and (r, 2p+1)
+  unsigned long long acc2[8][4];
 #pragma unroll
   for (int r = 0; r < 8; ++r)
 #pragma unroll
-    for (int c = 0; c < 8; ++c) acc[r][c] = 0.f;
+    for (int c = 0; c < 4; ++c) acc2[r][c] = 0ull;
   const int nchunks = a.D / kBK;
   float4 qn = qv ? __ldg(reinterpret_cast<const float4*>(qsrc)) : make_float4(0.f, 0.f, 0.f, 0.f);
   float4 kn = kv ? __ldg(reinterpret_cast<const float4*>(ksrc)) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -313,16 +314,29 @@ __global__ void __launch_bounds__(kThreads, 2) score_gemm_kernel(Args a) {
     for (int d = 0; d < kBK; ++d) {
       const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][d][ty * 4]);
       const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][d][64 + ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][d][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][d][64 + tx * 4]);
+      const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(&Bs[buf][d][tx * 4]);
+      const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(&Bs[buf][d][64 + tx * 4]);
       const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const unsigned long long bp[4] = {b0.x, b0.y, b1.x, b1.y};  // (b[2p], b[2p+1]) pairs
 #pragma unroll
-      for (int r = 0; r < 8; ++r)
+      for (int r = 0; r < 8; ++r) {
+        unsigned long long ap;  // (a[r], a[r])
+        asm("mov.b64 %0, {%1, %1};" : "=l"(ap) : "f"(av[r]));
 #pragma unroll
-        for (int c = 0; c < 8; ++c) acc[r][c] = __fmaf_rn(av[r], bv[c], acc[r][c]);
+        for (int c = 0; c < 4; ++c)
+          // two independent round-to-nearest fp32 FMAs: the same values as two fmaf calls
+          asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc2[r][c]) : "l"(ap), "l"(bp[c]));
+      }
     }
   }
+  float acc[8][8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      acc[r][2 * c] = __uint_as_float(static_cast<uint32_t>(acc2[r][c]));
+      acc[r][2 * c + 1] = __uint_as_float(static_cast<uint32_t>(acc2[r][c] >> 32));
+    }
   float* out = a.scores + static_cast<long long>(bh) * a.nq * a.ldc;
   const bool vec = (a.ldc & 3) == 0;
 #pragma unroll
