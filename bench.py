@@ -38,7 +38,7 @@ METRIC = "BSA sparse TFLOP/s (4*B*H*S*k*64*D per call) at the 720p refinement sh
 UNIT = "TFLOP/s"
 # DRAM bytes (read + write) of one attention launch per (batch, head) at the config-2 shape, from the ncu
 # capture summarised in profiles/bsa_kernels_config2_h4_full.md (426 MB for 4 heads; traffic is per head).
-ATTN_DRAM_BYTES_PER_HEAD = {"config2": (357.539328e6 + 76.882432e6) / 4}
+ATTN_DRAM_BYTES_PER_HEAD = {"config2": (319.036672e6 + 81.871872e6) / 4}
 
 
 def _peaks():

@@ -155,6 +155,14 @@ int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t 
   a.rope = rope; a.rope_dt = rope_dt; a.rope_dh = rope_dh; a.rope_dw = rope_dw;
   a.rope_T = rope_T; a.rope_H = rope_H; a.rope_W = rope_W;
   a.x_rot = x_rot; a.pooled = pooled;
+  // bf16/fp16 blocks of 64 d-wide halves stream through a TMA ring; the map needs mergeable batch
+  // and head strides, which the register kernel does not
+  CUtensorMap m;
+  a.tmap = nullptr;
+  if (dtype != BSA_DTYPE_F32 && (B == 1 || sb == static_cast<int64_t>(H) * sh)) {
+    const int64_t st[3] = {sb, sh, ss};
+    if (make_map(&m, x, dtype, B, H, D, st, T, Hl, Wl, cT, cH, cW, "x") == BSA_OK) a.tmap = &m;
+  }
   rc = bsa::launch_pool(a, static_cast<cudaStream_t>(stream));
   if (rc == BSA_ERR_CUDA) return cuda_fail("pool kernel launch");
   if (rc) return fail(rc, "pool: unsupported configuration");

@@ -20,6 +20,7 @@ struct PoolArgs {
   int rope_T, rope_H, rope_W;  // RoPE grid; token s sits at (s / (H*W), (s / W) % H, s % W)
   void* x_rot;           // [B,H,S,D] contiguous, same dtype as x (required when rope != null)
   float* pooled;         // [B*H, nb, D] fp32
+  const CUtensorMap* tmap;  // nullable: 5-D block map over x (bf16/fp16); selects the TMA-ring kernel
 };
 int launch_pool(const PoolArgs& a, cudaStream_t stream);
 

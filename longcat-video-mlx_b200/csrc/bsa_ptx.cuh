@@ -62,7 +62,7 @@ constexpr uint64_t kWaitLimitNs = 1000000000ull;
 // `err` (global) receives `site` (first timeout wins).
 // The spin after a first unsuccessful poll is kept out of line: the wait sites stay small in the
 // instruction stream of the hot loops.
-__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
                                             int site) {
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;

@@ -15,10 +15,12 @@
 // bound and keeps each score row on chip for the selection.
 #include <algorithm>
 #include <cstdint>
+#include <type_traits>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include "bsa_kernels.h"
+#include "bsa_ptx.cuh"
 
 namespace bsa {
 
@@ -215,7 +217,171 @@ __global__ void __launch_bounds__(kThreads, kRope ? 3 : 4)
     }
   }
 }
+// ------------------------------------------------------------------------ pooling through a TMA ring
+// The same pooling (without RoPE) for bf16/fp16 inputs, with the blocks streamed into shared memory by
+// TMA: one producer lane keeps up to kRing blocks (16 KB each) in flight per SM, and kConsumers warps
+// reduce them.  Row order and the fp32 pairwise tree are those of pool_kernel, so results are identical.
+constexpr int kConsumers = 8;
+constexpr int kTmaThreads = 32 * (kConsumers + 1);
+constexpr int kRing = 12;
+constexpr int kSlotBytes = 16384;  // two 8 KB d-halves of up to 64 rows x 128 B, 128B-swizzled
+struct RingSmem {
+  uint64_t full[kRing];
+  uint64_t empty[kRing];
+  int abort_flag;
+};
+constexpr int kTmaSmemBytes = 1024 + kRing * kSlotBytes + static_cast<int>(sizeof(RingSmem));
+
+// Four consecutive d values (lane's d0 .. d0+3) of row r from a 128B-swizzled block slot.
+template <typename T>
+__device__ __forceinline__ void slot_load4(const uint8_t* slot, int r, int lane, float (&v)[4]) {
+  const uint8_t* p = slot + (lane >> 4) * 8192 + sw128_offset(static_cast<uint32_t>(r), (lane & 15) >> 1) + 8 * (lane & 1);
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  if constexpr (sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value) {
+    v[0] = __uint_as_float(u.x << 16);
+    v[1] = __uint_as_float(u.x & 0xffff0000u);
+    v[2] = __uint_as_float(u.y << 16);
+    v[3] = __uint_as_float(u.y & 0xffff0000u);
+  } else {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTmaThreads, 1)
+    pool_tma_kernel(const __grid_constant__ CUtensorMap tm, float* pooled, Geo g) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* ring = smem_raw + ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw)) & 1023u)) & 1023u);
+  RingSmem& rs = *reinterpret_cast<RingSmem*>(ring + kRing * kSlotBytes);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  if (tid == 0) {
+    for (int i = 0; i < kRing; ++i) {
+      mbar_init(&rs.full[i], 1);
+      mbar_init(&rs.empty[i], 1);
+    }
+    rs.abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  volatile int* abort_flag = &rs.abort_flag;
+  const int total = g.B * g.H * g.nb;
+  const int per_t = g.Bh * g.Bw;
+  const int G = gridDim.x;
+  const int cnt = total > static_cast<int>(blockIdx.x) ? (total - 1 - static_cast<int>(blockIdx.x)) / G + 1 : 0;
+  const uint32_t box_bytes = static_cast<uint32_t>(g.n) * 128u;
+  if (warp == kConsumers) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      prefetch_tmap(&tm);
+      int i = 0;
+      for (; i < cnt; ++i) {
+        const int slot = i % kRing;
+        if (i >= kRing &&
+            !mbar_wait(&rs.empty[slot], static_cast<uint32_t>((i / kRing - 1) & 1), abort_flag, &g_score_err, 301))
+          break;
+        const int item = static_cast<int>(blockIdx.x) + i * G;
+        const int blk = item % g.nb;
+        const int bh = item / g.nb;
+        const int bt = blk / per_t;
+        const int rr = blk - bt * per_t;
+        const int bhh = rr / g.Bw;
+        const int bw = rr - bhh * g.Bw;
+        uint8_t* dst = ring + slot * kSlotBytes;
+        mbar_arrive_expect_tx(&rs.full[slot], 2u * box_bytes);
+        tma_load_5d(dst, &tm, &rs.full[slot], 0, bw * g.cW, bhh * g.cH, bt * g.cT, bh);
+        tma_load_5d(dst + 8192, &tm, &rs.full[slot], 64, bw * g.cW, bhh * g.cH, bt * g.cT, bh);
+      }
+      // teardown: no TMA write into this CTA's shared memory may still be in flight
+      const uint64_t t0 = globaltimer_ns();
+      for (int j = (i > kRing ? i - kRing : 0); j < i; ++j)
+        while (!mbar_try_wait(&rs.full[j % kRing], static_cast<uint32_t>((j / kRing) & 1)) &&
+               globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- consumers: warp w takes blocks w, w+8, ...
+    const int d0 = lane * 4;
+    const bool dact = d0 < g.D;
+    const float inv_n = 1.0f / static_cast<float>(g.n);
+    for (int i = warp; i < cnt; i += kConsumers) {
+      const int slot = i % kRing;
+      bool ok = mbar_wait(&rs.full[slot], static_cast<uint32_t>((i / kRing) & 1), abort_flag, &g_score_err, 302);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const uint8_t* sl = ring + slot * kSlotBytes;
+      const int item = static_cast<int>(blockIdx.x) + i * G;
+      const int blk = item % g.nb;
+      const int bh = item / g.nb;
+      // Pairwise tree in token order: each group of 8 rows is summed as its own subtree
+      // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)) in registers, and the 8-row sums are
+      // carried up a 3-level binary counter (warp-uniform branches, no dynamic indexing), which
+      // is the same sequence of fp32 additions as inserting the rows one by one.
+      float up0[4], up1[4], up2[4];
+      float tot[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int r0 = 0; r0 < g.n; r0 += 8) {
+        float v[8][4];
+#pragma unroll
+        for (int ii = 0; ii < 8; ++ii) {
+          if (r0 + ii < g.n) slot_load4<T>(sl, r0 + ii, lane, v[ii]);
+          else v[ii][0] = v[ii][1] = v[ii][2] = v[ii][3] = 0.f;
+        }
+        if (g.n < 8) {  // n = 1, 2 or 4: the whole tree is in this group
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p01 = __fadd_rn(v[0][e], v[1][e]);
+            tot[e] = g.n == 1 ? v[0][e] : (g.n == 2 ? p01 : __fadd_rn(p01, __fadd_rn(v[2][e], v[3][e])));
+          }
+          break;
+        }
+        float c[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          c[e] = __fadd_rn(__fadd_rn(__fadd_rn(v[0][e], v[1][e]), __fadd_rn(v[2][e], v[3][e])),
+                           __fadd_rn(__fadd_rn(v[4][e], v[5][e]), __fadd_rn(v[6][e], v[7][e])));
+        const int q = r0 >> 3;  // index of this 8-row group
+        if ((q & 1) == 0) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) up0[e] = c[e];
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) c[e] = __fadd_rn(up0[e], c[e]);
+          if ((q & 2) == 0) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) up1[e] = c[e];
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) c[e] = __fadd_rn(up1[e], c[e]);
+            if ((q & 4) == 0) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) up2[e] = c[e];
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) c[e] = __fadd_rn(up2[e], c[e]);
+            }
+          }
+        }
+        if (r0 + 8 == g.n) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) tot[e] = c[e];
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rs.empty[slot]);  // the slot's rows are in registers / written out
+      if (dact) {
+        const float out[4] = {__fmul_rn(tot[0], inv_n), __fmul_rn(tot[1], inv_n), __fmul_rn(tot[2], inv_n),
+                              __fmul_rn(tot[3], inv_n)};
+        store4(pooled + (static_cast<long long>(bh) * g.nb + blk) * g.D + d0, out);
+      }
+    }
+  }
+}
 }  // namespace pool
+
 
 int launch_pool(const PoolArgs& a, cudaStream_t stream) {
   using namespace pool;
@@ -238,6 +404,25 @@ int launch_pool(const PoolArgs& a, cudaStream_t stream) {
   if (grid < 1) return BSA_OK;
   dim3 gd(static_cast<unsigned>(grid), 1, 1);
   const bool rope = a.rope != nullptr;
+  if (a.tmap && !rope && (a.dtype == BSA_DTYPE_BF16 || a.dtype == BSA_DTYPE_F16)) {
+    // TMA ring: one persistent CTA per SM.  With fused RoPE the register kernel stays faster (its 32
+    // warps per SM hide the per-row table loads and the rotated-row stores; 1.77 vs 2.22 ms of routing)
+    static bool configured[64][2] = {};
+    const int ti = a.dtype == BSA_DTYPE_BF16 ? 0 : 1;
+    if (dev < 64 && !configured[dev][ti]) {
+      const cudaError_t e =
+          ti == 0 ? cudaFuncSetAttribute(pool_tma_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kTmaSmemBytes)
+                  : cudaFuncSetAttribute(pool_tma_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kTmaSmemBytes);
+      if (e != cudaSuccess) return BSA_ERR_CUDA;
+      configured[dev][ti] = true;
+    }
+    const dim3 tgd(static_cast<unsigned>(total < sms ? total : sms), 1, 1);
+    if (ti == 0) pool_tma_kernel<__nv_bfloat16><<<tgd, kTmaThreads, kTmaSmemBytes, stream>>>(*a.tmap, a.pooled, g);
+    else pool_tma_kernel<__half><<<tgd, kTmaThreads, kTmaSmemBytes, stream>>>(*a.tmap, a.pooled, g);
+    return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
+  }
 #define BSA_POOL_LAUNCH(TT)                                                                                      \
   do {                                                                                                           \
     if (rope)                                                                                                    \
@@ -380,6 +565,67 @@ struct Args {
   int32_t* idx;         // [rows, topk]
 };
 
+constexpr int kCand = 64;  // threshold candidates kept after the first radix digit
+
+// One radix digit (up to 8 bits below `shift`) over NK keys per lane: histogram of the keys that
+// match `prefix` above `shift`, then the digit whose bin holds the need-th largest key.  Updates
+// shift, prefix and need (keys still to take at or below the new prefix); `bincnt` receives the
+// count of the chosen bin (after the last digit: the number of keys equal to the threshold).
+template <int NK>
+__device__ __forceinline__ void radix_pass(const uint32_t (&key)[NK], uint32_t* h, int lane, int& shift,
+                                           uint32_t& prefix, int& need, uint32_t& bincnt) {
+  const int w = shift < 8 ? shift : 8;
+  const int hi_bits = shift;  // keys must match `prefix` above bit `shift`
+  shift -= w;
+  const uint32_t dmask = (1u << w) - 1u;
+  reinterpret_cast<uint4*>(h)[lane * 2] = make_uint4(0u, 0u, 0u, 0u);
+  reinterpret_cast<uint4*>(h)[lane * 2 + 1] = make_uint4(0u, 0u, 0u, 0u);
+  __syncwarp();
+#pragma unroll
+  for (int e = 0; e < NK; ++e) {
+    const uint32_t u = key[e];
+    const bool match = u != 0u && (hi_bits >= 32 || (u >> hi_bits) == (prefix >> hi_bits));
+    if (match) atomicAdd(&h[(u >> shift) & dmask], 1u);
+  }
+  __syncwarp();
+  const uint4 c0 = reinterpret_cast<const uint4*>(h)[lane * 2];
+  const uint4 c1 = reinterpret_cast<const uint4*>(h)[lane * 2 + 1];
+  const uint32_t cnt[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  uint32_t tot = 0;
+#pragma unroll
+  for (int b = 0; b < 8; ++b) tot += cnt[b];
+  uint32_t suf = tot;  // inclusive suffix sum over lanes >= this lane
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t o = __shfl_down_sync(0xffffffffu, suf, off);
+    if (lane + off < 32) suf += o;
+  }
+  const uint32_t above = suf - tot;
+  const bool mine = above < static_cast<uint32_t>(need) && static_cast<uint32_t>(need) <= suf;
+  int digit = 0;
+  uint32_t gt = 0, bc = 0;
+  if (mine) {
+    uint32_t run = above;
+#pragma unroll
+    for (int b = 7; b >= 0; --b) {
+      if (run + cnt[b] >= static_cast<uint32_t>(need)) {
+        digit = lane * 8 + b;
+        gt = run;
+        bc = cnt[b];
+        break;
+      }
+      run += cnt[b];
+    }
+  }
+  const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+  digit = __shfl_sync(0xffffffffu, digit, src);
+  gt = __shfl_sync(0xffffffffu, gt, src);
+  bincnt = __shfl_sync(0xffffffffu, bc, src);
+  prefix |= static_cast<uint32_t>(digit) << shift;
+  need -= static_cast<int>(gt);
+  __syncwarp();
+}
+
 // PL > 0: the row lives in registers (PL keys per lane, nk <= 32*PL); PL == 0: re-read from memory
 template <int PL>
 __global__ void __launch_bounds__(kThreads, 4) topk_kernel(Args a) {
@@ -409,11 +655,17 @@ __global__ void __launch_bounds__(kThreads, 4) topk_kernel(Args a) {
   };
   uint32_t T;
   int need;
+  uint32_t eqc = 0;  // number of keys equal to T (radix path)
   if constexpr (PL > 0) {
     // Radix select: 8-bit digits, starting below the bits that every key of the row shares
-    // (from the row's min and max key), counted in a per-warp shared histogram.
+    // (from the row's min and max key), counted in a per-warp shared histogram.  After the first
+    // digit only the keys of the chosen bin can still be the threshold; for rows of up to 48 keys
+    // per lane with at most kCand such keys, they are compacted (in index order) and the later
+    // digits run on those alone (385 -> 352 us at config 2).
     __shared__ __align__(16) uint32_t hist_all[kThreads / 32][256];
+    __shared__ uint32_t cand_all[kThreads / 32][kCand];
     uint32_t* h = hist_all[threadIdx.x >> 5];
+    uint32_t* cand = cand_all[threadIdx.x >> 5];
     uint32_t kmin = 0xffffffffu, kmax = 0u;
 #pragma unroll
     for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
@@ -427,55 +679,29 @@ __global__ void __launch_bounds__(kThreads, 4) topk_kernel(Args a) {
     int shift = 32 - __clz(kmin ^ kmax);  // low bits that still vary across the row
     uint32_t prefix = shift >= 32 ? 0u : (kmax & ~((1u << shift) - 1u));
     need = k;
-    while (shift > 0) {
-      const int w = shift < 8 ? shift : 8;
-      const int hi_bits = shift;  // keys must match `prefix` above bit `shift`
-      shift -= w;
-      const uint32_t dmask = (1u << w) - 1u;
-      reinterpret_cast<uint4*>(h)[lane * 2] = make_uint4(0u, 0u, 0u, 0u);
-      reinterpret_cast<uint4*>(h)[lane * 2 + 1] = make_uint4(0u, 0u, 0u, 0u);
-      __syncwarp();
+    eqc = static_cast<uint32_t>(nk);  // every key is equal when no bit varies
+    if (shift > 0) {
+      radix_pass<PL>(key, h, lane, shift, prefix, need, eqc);
+      if (PL <= 48 && shift > 0 && eqc <= static_cast<uint32_t>(kCand)) {  // measured: no gain at 96 keys
+        const uint32_t lt = (1u << lane) - 1u;
+        int pos = 0;
 #pragma unroll
-      for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
-        const uint32_t u = key[e];
-        const bool match = u != 0u && (hi_bits >= 32 || (u >> hi_bits) == (prefix >> hi_bits));
-        if (match) atomicAdd(&h[(u >> shift) & dmask], 1u);
-      }
-      __syncwarp();
-      const uint4 c0 = reinterpret_cast<const uint4*>(h)[lane * 2];
-      const uint4 c1 = reinterpret_cast<const uint4*>(h)[lane * 2 + 1];
-      const uint32_t cnt[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-      uint32_t tot = 0;
-#pragma unroll
-      for (int b = 0; b < 8; ++b) tot += cnt[b];
-      uint32_t suf = tot;  // inclusive suffix sum over lanes >= this lane
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const uint32_t o = __shfl_down_sync(0xffffffffu, suf, off);
-        if (lane + off < 32) suf += o;
-      }
-      const uint32_t above = suf - tot;
-      const bool mine = above < static_cast<uint32_t>(need) && static_cast<uint32_t>(need) <= suf;
-      int digit = 0;
-      uint32_t gt = 0;
-      if (mine) {
-        uint32_t run = above;
-#pragma unroll
-        for (int b = 7; b >= 0; --b) {
-          if (run + cnt[b] >= static_cast<uint32_t>(need)) {
-            digit = lane * 8 + b;
-            gt = run;
-            break;
-          }
-          run += cnt[b];
+        for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
+          const uint32_t u = key[e];
+          const bool m = u != 0u && (u >> shift) == (prefix >> shift);
+          const uint32_t mb = __ballot_sync(0xffffffffu, m);
+          if (m) cand[pos + __popc(mb & lt)] = u;
+          pos += __popc(mb);
         }
+        __syncwarp();
+        uint32_t ck[kCand / 32];
+#pragma unroll
+        for (int c = 0; c < kCand / 32; ++c) ck[c] = lane + 32 * c < pos ? cand[lane + 32 * c] : 0u;
+        __syncwarp();
+        while (shift > 0) radix_pass<kCand / 32>(ck, h, lane, shift, prefix, need, eqc);
+      } else {
+        while (shift > 0) radix_pass<PL>(key, h, lane, shift, prefix, need, eqc);
       }
-      const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
-      digit = __shfl_sync(0xffffffffu, digit, src);
-      gt = __shfl_sync(0xffffffffu, gt, src);
-      prefix |= static_cast<uint32_t>(digit) << shift;
-      need -= static_cast<int>(gt);
-      __syncwarp();
     }
     T = prefix;
   } else {
@@ -504,7 +730,18 @@ __global__ void __launch_bounds__(kThreads, 4) topk_kernel(Args a) {
     taken += __popc(sb);
     ties += __popc(eqb);
   };
-  if (PL > 0) {
+  if (PL > 0 && need == static_cast<int>(eqc)) {
+    // every key equal to T is taken: one ballot per 32 keys
+#pragma unroll
+    for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
+      if (32 * e >= nk) break;  // warp-uniform
+      const int j = lane + 32 * e;
+      const bool sel = j < nk && key[e] >= T;
+      const uint32_t sb = __ballot_sync(0xffffffffu, sel);
+      if (sel) out[taken + __popc(sb & lt_mask)] = j;
+      taken += __popc(sb);
+    }
+  } else if (PL > 0) {
 #pragma unroll
     for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
       if (32 * e >= nk) break;  // warp-uniform

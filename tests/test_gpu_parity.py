@@ -87,7 +87,9 @@ def test_pool_fused_rope_bitexact(cuda, dtype):
     assert _np(pooled).tobytes() == ref_pool.tobytes()
 
 
-@pytest.mark.parametrize("nb,D,k", [(64, 128, 4), (130, 128, 9), (200, 64, 1), (96, 40, 96), (1350, 128, 85)])
+# nb up to 1536 keeps a row in 48 registers per lane, up to 3072 in 96, longer rows are re-read from memory
+@pytest.mark.parametrize("nb,D,k", [(64, 128, 4), (130, 128, 9), (200, 64, 1), (96, 40, 96), (1350, 128, 85),
+                                    (2000, 32, 130), (3200, 16, 50)])
 def test_score_topk_bitexact(cuda, nb, D, k):
     from longcat_video import _native
 
