@@ -37,8 +37,21 @@ for _p in (REPO, PKG):
 METRIC = "BSA sparse TFLOP/s (4*B*H*S*k*64*D per call) at the 720p refinement shape"
 UNIT = "TFLOP/s"
 # DRAM bytes (read + write) of one attention launch per (batch, head) at the config-2 shape, from the ncu
-# capture summarised in profiles/bsa_kernels_config2_h4_full.md (426 MB for 4 heads; traffic is per head).
+# capture summarised in profiles/bsa_kernels_config2_h4_full.md (401 MB for 4 heads; traffic is per head).
 ATTN_DRAM_BYTES_PER_HEAD = {"config2": (319.036672e6 + 81.871872e6) / 4}
+# L2 -> SM rate of TMA gathers of 16 KB K/V blocks measured alone on this part (working sets of 8-100 MB): the
+# ceiling of the attention kernel's tile gather.
+TMA_GATHER_CEILING_TBS = 11.0
+
+
+def attn_gather_bytes(cfg, world: int = 1) -> float:
+    """Algorithmic L2 -> shared-memory bytes of one attention call on one rank: every (q-block, selected
+    kv-block) pair brings its own 64-token K and V tiles."""
+    import torch
+
+    elt = torch.empty((), dtype=cfg.dtype).element_size() if cfg.dtype != torch.float32 else 2  # f32 runs f16 attention
+    nb = cfg.S // 64
+    return float(cfg.B * (cfg.H // world) * nb * cfg.topk * 2 * 64 * cfg.D * elt)
 
 
 def _peaks():
@@ -405,6 +418,7 @@ def run_ours(args, cfg):
         flops_local = cfg.sparse_flops() / world
         achieved = flops_local / (attn_avg * 1e-3) / 1e12
         per_head = ATTN_DRAM_BYTES_PER_HEAD.get(cfg.name)
+        gbytes = attn_gather_bytes(cfg, world)
         traffic = per_head * cfg.B * (cfg.H // world) if per_head else None
         cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
         cpu = None
@@ -433,7 +447,12 @@ def run_ours(args, cfg):
                          "frac_of_sustained": achieved / peak_tf_sus, "kernel": "bsa_attn_kernel",
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 4-head capture "
                                            "scaled per head (profiles/bsa_kernels_config2_h4_full.md)"
-                         if traffic else None},
+                         if traffic else None,
+                         # the resource the kernel actually runs against: the K/V tile gather from L2
+                         "gather": {"unit": "TB/s", "bytes": gbytes, "achieved": gbytes / (attn_avg * 1e-3) / 1e12,
+                                    "ceiling": TMA_GATHER_CEILING_TBS,
+                                    "frac": gbytes / (attn_avg * 1e-3) / 1e12 / TMA_GATHER_CEILING_TBS,
+                                    "ceiling_kind": "measured TMA gather of 16 KB blocks from L2"}},
             "e2e": {"value": cfg.sparse_flops() / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             # per step: pool Q, pool K, score GEMM, top-k, attention

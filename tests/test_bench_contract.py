@@ -24,3 +24,18 @@ def test_reference_arm_prints_contract_line():
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["config"]["workload"] == "config2"
+
+
+def test_gather_roofline_bytes():
+    """The attention gather roofline counts one 64-token K and V tile pair per (q-block, selected kv-block);
+    fp32 configs run their attention in fp16."""
+    sys.path.insert(0, REPO)
+    sys.path.insert(0, os.path.join(REPO, "longcat-video-mlx_b200"))
+    import bench
+    from longcat_video.workloads import CONFIGS
+
+    c2 = CONFIGS["config2"]
+    assert bench.attn_gather_bytes(c2) == 32 * 1350 * 85 * 2 * 64 * 128 * 2
+    assert bench.attn_gather_bytes(c2, 4) == bench.attn_gather_bytes(c2) / 4
+    c1 = CONFIGS["config1"]
+    assert bench.attn_gather_bytes(c1) == c1.B * c1.H * (c1.S // 64) * c1.topk * 2 * 64 * c1.D * 2
