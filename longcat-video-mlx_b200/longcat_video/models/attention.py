@@ -78,13 +78,15 @@ class Attention(torch.nn.Module):
         return F.scaled_dot_product_attention(q, k, v, scale=self.scale)
 
     def forward(self, x: torch.Tensor, shape: Tuple[int, int, int],
-                num_cond_latents: Optional[int] = None) -> torch.Tensor:
-        """attention.py:181-233.  x: [B, N, C] -> [B, N, C]."""
+                num_cond_latents: Optional[int] = None, return_kv: bool = False):
+        """attention.py:181-233.  x: [B, N, C] -> [B, N, C].  With ``return_kv`` also returns the
+        (k, v) of this call for a later :meth:`forward_with_kv_cache`: k after RMSNorm, before RoPE."""
         B, N, C = x.shape
         qkv = self.qkv(x).reshape(B, N, 3, self.num_heads, self.head_dim).permute(2, 0, 3, 1, 4)
         q, k, v = qkv[0], qkv[1], qkv[2]
         q = self.q_norm(q)
         k = self.k_norm(k)
+        kv = (k, v) if return_kv else None
         if num_cond_latents is not None and num_cond_latents > 0:
             q, k = self.rope_3d(q, k, shape)
             ncl = num_cond_latents * (N // shape[0])
@@ -94,5 +96,30 @@ class Attention(torch.nn.Module):
             out = torch.cat([x_cond, x_noise], dim=2)
         else:
             out = self._process_attn(q, k, v, shape=shape, rope_grid=shape)
-        out = out.transpose(1, 2).reshape(B, N, C)
-        return self.proj(out)
+        out = self.proj(out.transpose(1, 2).reshape(B, N, C))
+        return (out, kv) if return_kv else out
+
+    def forward_with_kv_cache(self, x: torch.Tensor, shape: Tuple[int, int, int], num_cond_latents: Optional[int],
+                              kv_cache: Tuple[torch.Tensor, torch.Tensor]) -> torch.Tensor:
+        """attention.py:235-275: chunked continuation.  The fresh K/V are appended to the cached ones
+        (a cache stored at batch 1 is broadcast to B).  With conditioning latents, q is padded with zeros
+        over the cache positions so that RoPE over the extended grid (T + num_cond_latents, H, W) gives
+        q and k their global positions.  Q and KV lengths differ, so the hook takes its dense path."""
+        B, N, C = x.shape
+        qkv = self.qkv(x).reshape(B, N, 3, self.num_heads, self.head_dim).permute(2, 0, 3, 1, 4)
+        q, k, v = qkv[0], qkv[1], qkv[2]
+        q = self.q_norm(q)
+        k = self.k_norm(k)
+        T, Hl, Wl = shape
+        k_cache, v_cache = kv_cache
+        if k_cache.shape[0] == 1 and B > 1:
+            k_cache = k_cache.expand(B, *k_cache.shape[1:])
+            v_cache = v_cache.expand(B, *v_cache.shape[1:])
+        k_full = torch.cat([k_cache, k], dim=2)
+        v_full = torch.cat([v_cache, v], dim=2)
+        if num_cond_latents is not None and num_cond_latents > 0:
+            q_pad = torch.cat([torch.zeros_like(k_cache), q], dim=2)
+            q_pad, k_full = self.rope_3d(q_pad, k_full, (T + num_cond_latents, Hl, Wl))
+            q = q_pad[:, :, -N:]
+        out = self._process_attn(q, k_full, v_full, shape=None)
+        return self.proj(out.transpose(1, 2).reshape(B, N, C))

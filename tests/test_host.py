@@ -196,3 +196,43 @@ def test_head_group_choice():
     assert _head_groups(8, 8, None) == 1
     assert _head_groups(32, 8, 3) == 2  # 32/3 does not split; 2 groups of 16 heads do
     assert _head_groups(24, 8, 2) == 1  # 12 heads per group do not split over 8 ranks
+
+
+def test_kv_cache_continuation_matches_full_forward():
+    """attention.py:235-275: continuing from the cached (k, v) of the conditioning frames gives the noise rows
+    of the one-shot cond + noise forward (same RoPE positions, same dense attention), also when a batch-1
+    cache is broadcast to batch 2."""
+    from longcat_video.models.attention import Attention
+
+    torch.manual_seed(0)
+    attn = Attention(64, 2).float()
+    T, Hl, Wl, ncl = 4, 2, 3, 2
+    nc = ncl * Hl * Wl
+    x = torch.randn(2, T * Hl * Wl, 64)
+    x[1, :nc] = x[0, :nc]  # one conditioning clip for both batch rows
+    with torch.no_grad():
+        full = attn(x, (T, Hl, Wl), num_cond_latents=ncl)
+        for cache_batch in (2, 1):
+            out_c, kv = attn(x[:cache_batch, :nc], (ncl, Hl, Wl), return_kv=True)
+            assert out_c.shape == (cache_batch, nc, 64) and kv[0].shape == (cache_batch, 2, nc, 32)
+            cont = attn.forward_with_kv_cache(x[:, nc:], (T - ncl, Hl, Wl), ncl, kv)
+            torch.testing.assert_close(cont, full[:, nc:], rtol=1e-5, atol=1e-6)
+
+
+def test_kv_cache_continuation_without_cond_skips_rope():
+    """Without conditioning latents the continuation attends the fresh queries to cache + fresh keys with no
+    RoPE, as the reference does (attention.py:266-268)."""
+    import torch.nn.functional as F
+    from longcat_video.models.attention import Attention
+
+    torch.manual_seed(1)
+    attn = Attention(32, 2).float()
+    x_prev, x = torch.randn(1, 6, 32), torch.randn(1, 4, 32)
+    with torch.no_grad():
+        _, kv = attn(x_prev, (1, 2, 3), return_kv=True)
+        got = attn.forward_with_kv_cache(x, (1, 2, 2), 0, kv)
+        qkv = attn.qkv(x).reshape(1, 4, 3, 2, 16).permute(2, 0, 3, 1, 4)
+        q, k, v = attn.q_norm(qkv[0]), attn.k_norm(qkv[1]), qkv[2]
+        o = F.scaled_dot_product_attention(q, torch.cat([kv[0], k], 2), torch.cat([kv[1], v], 2), scale=attn.scale)
+        want = attn.proj(o.transpose(1, 2).reshape(1, 4, 32))
+    torch.testing.assert_close(got, want)
