@@ -130,6 +130,16 @@ def _strides(t: torch.Tensor):
     return arr
 
 
+def _merge_batch(t: torch.Tensor) -> torch.Tensor:
+    """The attention kernel reads q/k/v through one 5-D TMA map whose last axis is b*H + h, so for B > 1
+    the batch stride must equal H times the head stride.  Views that break this (the DiT's
+    ``reshape(B, N, 3, H, D).permute(2, 0, 3, 1, 4)`` at B > 1) are copied once to a contiguous layout;
+    everything else is used in place."""
+    if t.dim() == 4 and t.shape[0] > 1 and t.stride(0) != t.shape[1] * t.stride(1):
+        return t.contiguous()
+    return t
+
+
 def _dtype_code(t: torch.Tensor) -> int:
     try:
         return DTYPE_CODES[t.dtype]
@@ -244,6 +254,7 @@ def attention_indices(q, k, v, block_indices, shape, chunk_thw, sm_scale: float,
         return out
     if out is None:
         out = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
+    q, k, v = _merge_batch(q), _merge_batch(k), _merge_batch(v)
     rc = lib().bsa_attention_indices(q.data_ptr(), k.data_ptr(), v.data_ptr(), bi.data_ptr(), _dtype_code(q), B, H, S,
                                      D, _strides(q), _strides(k), _strides(v), T, H_, W, cT, cH, cW, int(bi.shape[-1]),
                                      float(sm_scale), out.data_ptr(), _strides(out), _stream(q))
@@ -278,6 +289,7 @@ def _forward_f32(q, k, v, shape, chunk_thw, topk, sm_scale, rope, out, block_ind
 
 
 def _attention_ex(q, k, v, bi, shape, chunk_thw, sm_scale, out, sm_reserve):
+    q, k, v = _merge_batch(q), _merge_batch(k), _merge_batch(v)
     B, H, S, D = q.shape
     T, H_, W, cT, cH, cW = _geometry(S, shape, chunk_thw)
     rc = lib().bsa_attention_indices_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), bi.data_ptr(), _dtype_code(q), B,
@@ -302,6 +314,7 @@ def forward(q, k, v, shape, chunk_thw, topk: int, sm_scale: float, rope: Optiona
     nb = S // (cT * cH * cW)
     if q.dtype == torch.float32:
         return _forward_f32(q, k, v, shape, chunk_thw, topk, sm_scale, rope, out, block_indices, sm_reserve)
+    q, k, v = _merge_batch(q), _merge_batch(k), _merge_batch(v)
     if out is None:
         out = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
     if block_indices is None:

@@ -192,6 +192,19 @@ def test_attention_all_blocks_equals_dense(cuda):
     _close(_np(out), _np(dense))
 
 
+def test_batched_dit_views_run_sparse(cuda):
+    """B > 1 DiT views (batch and head strides that do not merge) run the sparse path, not a shape error."""
+    from longcat_video.models.block_sparse_attention import bsa_attention
+
+    B, N, H, D = 2, 512, 3, 128
+    qkv = _rand((B, N, 3, H, D), torch.bfloat16, 76, cuda).permute(2, 0, 3, 1, 4)
+    q, k, v = qkv[0], qkv[1], qkv[2]
+    a, ia = bsa_attention(q, k, v, (8, 8, 8), chunk_thw=(4, 4, 4), topk=3, return_indices=True)
+    b, ib = bsa_attention(q.contiguous(), k.contiguous(), v.contiguous(), (8, 8, 8), chunk_thw=(4, 4, 4), topk=3,
+                          return_indices=True)
+    assert torch.equal(ia, ib) and torch.equal(a, b)
+
+
 def test_attention_strided_inputs_match_contiguous(cuda):
     from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
 

@@ -236,3 +236,22 @@ def test_kv_cache_continuation_without_cond_skips_rope():
         o = F.scaled_dot_product_attention(q, torch.cat([kv[0], k], 2), torch.cat([kv[1], v], 2), scale=attn.scale)
         want = attn.proj(o.transpose(1, 2).reshape(1, 4, 32))
     torch.testing.assert_close(got, want)
+
+
+def test_batched_dit_views_are_merged_before_the_kernel():
+    """The attention kernel's TMA map merges batch and heads (stride(0) == H * stride(1)).  The DiT's
+    qkv.reshape(B, N, 3, H, D).permute(2, 0, 3, 1, 4) views break that at B > 1 and are copied once;
+    B = 1 views and mergeable tensors are used in place (no copy)."""
+    from longcat_video import _native
+
+    B, N, H, D = 2, 128, 4, 32
+    qkv = torch.randn(B, N, 3, H, D).permute(2, 0, 3, 1, 4)
+    q = qkv[0]
+    m = _native._merge_batch(q)
+    assert m.stride(0) == H * m.stride(1) and torch.equal(m, q) and m.data_ptr() != q.data_ptr()
+    q1 = torch.randn(1, N, 3, H, D).permute(2, 0, 3, 1, 4)[0]
+    assert _native._merge_batch(q1) is q1
+    c = torch.randn(B, H, N, D)
+    assert _native._merge_batch(c) is c
+    heads_view = torch.randn(B, 2 * H, N, D)[:, :H]  # a head slice keeps stride(0) = 2H * stride(1)
+    assert _native._merge_batch(heads_view).stride(0) == H * heads_view.stride(1)
