@@ -11,8 +11,9 @@
 //   pooling : pairwise tree over the n tokens of a block in token order ((r0 + r1) + (r2 + r3)) + ...,
 //             then * 1/n
 //   score   : one fma chain per score over d = 0..D-1 (fmaf(q[d], k[d], acc), acc starting at 0)
-// The pool kernel is HBM-bound (one read of Q and K); the score kernel is FMA/shared-memory
-// bound and keeps each score row on chip for the selection.
+// Pooling is HBM-bound (one read of Q and K; bf16/fp16 blocks stream through a TMA ring). The score
+// kernel is FMA-bound and writes the score matrix to the caller's scratch. The top-k kernel reads it
+// back one row per warp.
 #include <algorithm>
 #include <cstdint>
 #include <type_traits>
