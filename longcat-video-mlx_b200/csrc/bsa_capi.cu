@@ -160,8 +160,12 @@ int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t 
   CUtensorMap m;
   a.tmap = nullptr;
   if (dtype != BSA_DTYPE_F32 && (B == 1 || sb == static_cast<int64_t>(H) * sh)) {
+    // a map that cannot be built only selects the register kernel: keep the caller's last message
+    char saved[sizeof(g_msg)];
+    memcpy(saved, g_msg, sizeof(g_msg));
     const int64_t st[3] = {sb, sh, ss};
     if (make_map(&m, x, dtype, B, H, D, st, T, Hl, Wl, cT, cH, cW, "x") == BSA_OK) a.tmap = &m;
+    else memcpy(g_msg, saved, sizeof(g_msg));
   }
   rc = bsa::launch_pool(a, static_cast<cudaStream_t>(stream));
   if (rc == BSA_ERR_CUDA) return cuda_fail("pool kernel launch");
