@@ -5,7 +5,9 @@
  * asynchronously on that stream and returns a status code (BSA_OK == 0).  Nothing here
  * allocates device memory: outputs and scratch are owned by the caller.  Inputs are borrowed
  * read-only.  The error message of the last failing call on the calling host thread is
- * available from bsa_last_error().
+ * available from bsa_last_error().  Every entry point checks all of its arguments (and builds
+ * every TMA descriptor it needs) before it queues its first kernel: a call that returns an
+ * argument error (SHAPE, DTYPE, ALIGN, ARG) has launched nothing.
  *
  * Tensor conventions (the reference's, longcat_video/models/block_sparse_attention.py):
  *   q, k, v, out : [B, H, S, D] with element strides (sb, sh, ss) and d contiguous,
@@ -132,9 +134,12 @@ int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B
  * Calls that would need more (bsa_forward_scratch_bytes() > BSA_NOALLOC_SCRATCH_BYTES) return
  * BSA_ERR_SHAPE.  Nothing is allocated: no cudaMalloc, cudaFree or allocating library routine.
  * The first call on a device resolves the array's device address (cudaGetSymbolAddress, with that
- * device current); make that first call before any stream capture.  Every call on a device shares
- * the one array: calls whose kernels overlap on the GPU (different streams, or concurrent host
- * threads) race on it and must be serialised by the caller. */
+ * device current) and keeps it for the life of the process; make that first call before any stream
+ * capture.  A device reset (cudaDeviceReset) is not supported: the cached address would be stale.
+ * Every call on a device shares the one array: calls whose kernels overlap on the GPU (different
+ * streams, or concurrent host threads) race on it and must be serialised by the caller.  The array
+ * serves calls with 4*B*H*nb*(2*D + round_up(nb, 4)) <= BSA_NOALLOC_SCRATCH_BYTES (nb = S/64), i.e.
+ * small shapes; the 720p benchmark shapes need far more and are refused. */
 #define BSA_NOALLOC_SCRATCH_BYTES (16u << 20)
 int bsa_forward_noalloc(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
                         const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl,

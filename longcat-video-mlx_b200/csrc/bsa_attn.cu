@@ -33,6 +33,7 @@
 // Every mbarrier wait is bounded (bsa_ptx.cuh); a timeout records an error code and the CTA winds
 // down.
 #include <cstdint>
+#include <mutex>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include "bsa_ptx.cuh"
@@ -107,6 +108,7 @@ struct Params {
   float scale_log2;
   int total_units;
   int vec_out;          // out rows may be written with 16-byte stores
+  int map3;             // blocks are contiguous 64-token runs: q/k/v maps are 3-D (d, s, b*h)
 };
 
 __device__ int g_attn_err;
@@ -146,6 +148,12 @@ __device__ long long g_bsa_prof[1024][24][8];
   } while (0)
 #endif
 
+// One 64-wide d-half (c0 = 0 or 64) of block b of (b, h) slice bh into shared memory.  Blocks that are
+// contiguous runs of 64 tokens are read through a 3-D map (d, s, b*h) at token 64*b, which spares the
+// single issuing thread the divisions of the block's (t, h, w) origin; voxel blocks use the 5-D map.
+__device__ __forceinline__ void tma_block(const Params& p, void* dst, const CUtensorMap* m, uint64_t* bar, int c0,
+                                          int b, int bh);
+
 __device__ __forceinline__ void block_origin(const Params& p, int b, int& t0, int& h0, int& w0) {
   const int per_t = p.Bh * p.Bw;
   const int bt = b / per_t;
@@ -155,6 +163,17 @@ __device__ __forceinline__ void block_origin(const Params& p, int b, int& t0, in
   t0 = bt * p.cT;
   h0 = bh * p.cH;
   w0 = bw * p.cW;
+}
+
+__device__ __forceinline__ void tma_block(const Params& p, void* dst, const CUtensorMap* m, uint64_t* bar, int c0,
+                                          int b, int bh) {
+  if (p.map3) {
+    tma_load_3d(dst, m, bar, c0, b * kBlock, bh);
+  } else {
+    int t0, h0, w0;
+    block_origin(p, b, t0, h0, w0);
+    tma_load_5d(dst, m, bar, c0, w0, h0, t0, bh);
+  }
 }
 
 // Block ids of step j of a unit (the second id duplicates the first for an odd tail; those keys
@@ -338,12 +357,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           return false;
         const int bh = u / p.nqb;
         const int qblk = u - bh * p.nqb;
-        int t0, h0, w0;
-        block_origin(p, qblk, t0, h0, w0);
         mbar_arrive_expect_tx(&ss.q_full[qb], kQBytes);
         uint8_t* dst = sQ + qb * kQBytes;
-        tma_load_5d(dst, &tm_q, &ss.q_full[qb], 0, w0, h0, t0, bh);
-        tma_load_5d(dst + kQBytes / 2, &tm_q, &ss.q_full[qb], 64, w0, h0, t0, bh);
+        tma_block(p, dst, &tm_q, &ss.q_full[qb], 0, qblk, bh);
+        tma_block(p, dst + kQBytes / 2, &tm_q, &ss.q_full[qb], 64, qblk, bh);
         return true;
       };
       long long g = 0;
@@ -372,13 +389,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* dst = sK + ks * kPairBytes;
           mbar_arrive_expect_tx(&ss.k_full[ks], kPairBytes);
 #pragma unroll
-          for (int bi = 0; bi < 2; ++bi) {
-            int t0, h0, w0;
-            block_origin(p, bi ? b1 : b0, t0, h0, w0);
+          for (int bi = 0; bi < 2; ++bi)
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh)
-              tma_load_5d(dst + hh * 16384 + bi * 8192, &tm_k, &ss.k_full[ks], hh * 64, w0, h0, t0, bh);
-          }
+              tma_block(p, dst + hh * 16384 + bi * 8192, &tm_k, &ss.k_full[ks], hh * 64, bi ? b1 : b0, bh);
         }
       }
       // teardown: no TMA write into this CTA's shared memory may still be in flight
@@ -415,12 +429,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (gb >= kVSlots) ok = mbar_wait(&ss.v_empty[vs], vp.phase ^ 1u, abort_flag, err, 103, PACC(0));
             if (!ok) break;
             vp.next();
-            int t0, h0, w0;
-            block_origin(p, bi ? b1 : b0, t0, h0, w0);
             uint8_t* dst = sV + vs * kVBlockBytes;
             mbar_arrive_expect_tx(&ss.v_full[vs], kVBlockBytes);
-            tma_load_5d(dst, &tm_v, &ss.v_full[vs], 0, w0, h0, t0, bh);
-            tma_load_5d(dst + kVBlockBytes / 2, &tm_v, &ss.v_full[vs], 64, w0, h0, t0, bh);
+            tma_block(p, dst, &tm_v, &ss.v_full[vs], 0, bi ? b1 : b0, bh);
+            tma_block(p, dst + kVBlockBytes / 2, &tm_v, &ss.v_full[vs], 64, bi ? b1 : b0, bh);
           }
         }
       }
@@ -645,18 +657,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           ss.st_l[ub][h][row] = active ? l_half : 0.f;
         }
       }
-      // both halves' last PVs of this unit must be complete before O is read; each half has run
-      // the same number of steps in every unit, so the last step of either is known from n
+      // both halves' last PVs of this unit must be complete before O is read.  Each warp waits for its
+      // own half's last PV only (i - 1: steps of this half so far), in order; the ep handshake below
+      // carries the other half's.  Waiting on the other half's barrier here could run a whole phase
+      // ahead of it (that half may still be two PVs behind), which a parity wait misreads as done.
       bool w = true;
-      {
-        const long long done0 = static_cast<long long>(n + 1) * ((nsteps + 1) >> 1);
-        const long long done1 = static_cast<long long>(n + 1) * (nsteps >> 1);
-        const long long l0 = done0 - 1;
-        w = mbar_wait(&ss.p_empty[0][l0 & 1], static_cast<uint32_t>((l0 >> 1) & 1), abort_flag, err, 125);
-        if (w && two_halves) {
-          const long long l1 = done1 - 1;
-          w = mbar_wait(&ss.p_empty[1][l1 & 1], static_cast<uint32_t>((l1 >> 1) & 1), abort_flag, err, 126);
-        }
+      if (active) {
+        const long long last = i - 1;
+        w = mbar_wait(&ss.p_empty[h][last & 1], static_cast<uint32_t>((last >> 1) & 1), abort_flag, err, 125);
       }
       __syncwarp();
       if (lane == 0 && w) mbar_arrive(&ss.ep[qq]);
@@ -717,16 +725,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 int launch_attn(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, const AttnArgs& a,
                 cudaStream_t stream) {
   using namespace attn;
+  // the shared-memory opt-in is per device; first calls from several host threads may race here
+  static std::mutex mu;
   static bool configured[64] = {false};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(bsa_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(bsa_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
-            cudaSuccess)
-      return BSA_ERR_CUDA;
-    configured[dev] = true;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BSA_ERR_CUDA;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 64 || !configured[dev]) {
+      if (cudaFuncSetAttribute(bsa_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+              cudaSuccess ||
+          cudaFuncSetAttribute(bsa_attn_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+              cudaSuccess)
+        return BSA_ERR_CUDA;
+      if (dev < 64) configured[dev] = true;
+    }
   }
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -751,6 +764,7 @@ int launch_attn(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensor
   p.out_ss = a.out_ss;
   p.scale_log2 = a.sm_scale * 1.4426950408889634f;
   p.total_units = p.BH * a.nb;
+  p.map3 = a.map3;
   p.vec_out = ((reinterpret_cast<uintptr_t>(a.out) & 15u) == 0 && (a.out_ss * 2) % 16 == 0 &&
                (a.out_sh * 2) % 16 == 0 && (a.out_sb * 2) % 16 == 0)
                   ? 1

@@ -1,5 +1,10 @@
 // C ABI of the BSA engine (declared in include/bsa_b200.h): argument validation, TMA tensor-map
 // construction and kernel composition.  No entry point allocates device memory.
+//
+// Every entry point validates all of its arguments -- and builds every tensor map it will use --
+// before it queues its first kernel: a call that returns an error has launched nothing.  The work of
+// an entry point is therefore split into a plan (checks, maps, kernel arguments; host only) and a
+// run (the launches).
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -58,10 +63,21 @@ int check_geometry(int S, int T, int Hl, int Wl, int cT, int cH, int cW) {
   return BSA_OK;
 }
 
-// 5-D tiled map over one of q/k/v: dims (d, w, h, t, b*h), box (64, cW, cH, cT, 1), 128B swizzle.
-// Out-of-range d (D < 128) reads as zero, which pads the head dimension for the MMA.
+// A block of chunk_thw voxels is one contiguous run of tokens (in t-major order) when it spans whole
+// rows below its first partial axis: blocks are then numbered in token order, block b starting at
+// token b * cT*cH*cW.  The benchmark's 64-token blocks (shape (1, 1, S), chunk (1, 1, 64)) are.
+bool contiguous_blocks(int Hl, int Wl, int cT, int cH, int cW) {
+  return (cT == 1 || (cH == Hl && cW == Wl)) && (cH == 1 || cW == Wl);
+}
+
+// Tiled map over one of q/k/v, 128B swizzle, 64-element d halves.  Contiguous blocks: 3-D (d, s, b*h),
+// box (64, n, 1), addressed by the block's first token; other voxel blocks: 5-D (d, w, h, t, b*h), box
+// (64, cW, cH, cT, 1), addressed by the block's (t, h, w) origin.  Both move the same bytes at the same
+// rate (16 KB blocks gathered from L2: 13.4 TB/s either way); the 3-D form spares the issuing threads
+// the two integer divisions of the block origin.  Out-of-range d (D < 128) reads as zero, which pads
+// the head dimension for the MMA.  *map3 (nullable) receives which form was built.
 int make_map(CUtensorMap* m, const void* base, int dtype, int B, int H, int D, const int64_t* st, int T, int Hl,
-             int Wl, int cT, int cH, int cW, const char* name) {
+             int Wl, int cT, int cH, int cW, const char* name, int* map3 = nullptr) {
   auto enc = encode_fn();
   if (!enc) return fail(BSA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const int e = elt_bytes(dtype);
@@ -72,23 +88,46 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int B, int H, int D, c
                 name, (long long)sb, (long long)sh, (long long)ss);
   if (B > 1 && sb != static_cast<int64_t>(H) * sh)
     return fail(BSA_ERR_SHAPE, "%s: batch and head strides must merge (sb == H*sh) when B > 1", name);
-  cuuint64_t dims[5] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(Wl), static_cast<cuuint64_t>(Hl),
-                        static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(B) * H};
-  cuuint64_t strides[4] = {static_cast<cuuint64_t>(ss * e), static_cast<cuuint64_t>(ss * e * Wl),
-                           static_cast<cuuint64_t>(ss * e * Wl * Hl), static_cast<cuuint64_t>(sh * e)};
-  cuuint32_t box[5] = {64, static_cast<cuuint32_t>(cW), static_cast<cuuint32_t>(cH), static_cast<cuuint32_t>(cT), 1};
+  const bool c3 = contiguous_blocks(Hl, Wl, cT, cH, cW);
+  const cuuint64_t S = static_cast<cuuint64_t>(T) * Hl * Wl;
+  cuuint64_t dims[5], strides[4];
+  cuuint32_t box[5];
   cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  cuuint32_t rank;
+  if (c3) {
+    rank = 3;
+    dims[0] = static_cast<cuuint64_t>(D); dims[1] = S; dims[2] = static_cast<cuuint64_t>(B) * H;
+    strides[0] = static_cast<cuuint64_t>(ss * e); strides[1] = static_cast<cuuint64_t>(sh * e);
+    box[0] = 64; box[1] = static_cast<cuuint32_t>(cT * cH * cW); box[2] = 1;
+  } else {
+    rank = 5;
+    dims[0] = static_cast<cuuint64_t>(D); dims[1] = static_cast<cuuint64_t>(Wl); dims[2] = static_cast<cuuint64_t>(Hl);
+    dims[3] = static_cast<cuuint64_t>(T); dims[4] = static_cast<cuuint64_t>(B) * H;
+    strides[0] = static_cast<cuuint64_t>(ss * e); strides[1] = static_cast<cuuint64_t>(ss * e * Wl);
+    strides[2] = static_cast<cuuint64_t>(ss * e * Wl * Hl); strides[3] = static_cast<cuuint64_t>(sh * e);
+    box[0] = 64; box[1] = static_cast<cuuint32_t>(cW); box[2] = static_cast<cuuint32_t>(cH);
+    box[3] = static_cast<cuuint32_t>(cT); box[4] = 1;
+  }
   const CUtensorMapDataType dt =
       dtype == BSA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const CUresult r = enc(m, dt, 5, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  const CUresult r = enc(m, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (map3) *map3 = c3 ? 1 : 0;
   if (r != CUDA_SUCCESS) return fail(BSA_ERR_ARG, "%s: cuTensorMapEncodeTiled failed (%d)", name, static_cast<int>(r));
   return BSA_OK;
 }
 
-int check_pool_args(const void* x, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss, int T,
-                    int Hl, int Wl, int cT, int cH, int cW, float* pooled) {
+// ------------------------------------------------------------------ plans: validated, ready to launch
+struct PoolPlan {
+  bsa::PoolArgs a;
+  CUtensorMap map;
+  bool has_map = false;
+};
+
+int pool_plan(PoolPlan& pl, const void* x, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss,
+              int T, int Hl, int Wl, int cT, int cH, int cW, const float* rope, int rope_dt, int rope_dh, int rope_dw,
+              int rope_T, int rope_H, int rope_W, void* x_rot, float* pooled) {
   if (!x || !pooled) return fail(BSA_ERR_ARG, "null pointer");
   if (dtype != BSA_DTYPE_F32 && dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
     return fail(BSA_ERR_DTYPE, "unsupported dtype code %d", dtype);
@@ -101,8 +140,90 @@ int check_pool_args(const void* x, int dtype, int B, int H, int S, int D, int64_
   const int e = elt_bytes(dtype);
   if (!aligned16(x) || (ss * e) % 16 || (sh * e) % 16 || (sb * e) % 16)
     return fail(BSA_ERR_ALIGN, "x must be 16-byte aligned with 16-byte-multiple strides");
+  if (!aligned16(pooled)) return fail(BSA_ERR_ALIGN, "pooled must be 16-byte aligned");
+  if (rope) {
+    if (!x_rot) return fail(BSA_ERR_ARG, "x_rot is required with rope tables");
+    if (!aligned16(x_rot)) return fail(BSA_ERR_ALIGN, "x_rot must be 16-byte aligned");
+    if (rope_dt + rope_dh + rope_dw != D || (rope_dt | rope_dh | rope_dw) & 1 || rope_dt < 0 || rope_dh < 0 ||
+        rope_dw < 0)
+      return fail(BSA_ERR_SHAPE, "rope dims (%d, %d, %d) must be even and sum to D=%d", rope_dt, rope_dh, rope_dw, D);
+    if (rope_T <= 0 || rope_H <= 0 || rope_W <= 0 || static_cast<long long>(rope_T) * rope_H * rope_W != S)
+      return fail(BSA_ERR_SHAPE, "rope grid (%d, %d, %d) does not cover S=%d", rope_T, rope_H, rope_W, S);
+  }
+  bsa::PoolArgs& a = pl.a;
+  a.x = x; a.dtype = dtype; a.B = B; a.H = H; a.S = S; a.D = D; a.sb = sb; a.sh = sh; a.ss = ss;
+  a.T = T; a.Hl = Hl; a.Wl = Wl; a.cT = cT; a.cH = cH; a.cW = cW;
+  a.rope = rope; a.rope_dt = rope_dt; a.rope_dh = rope_dh; a.rope_dw = rope_dw;
+  a.rope_T = rope_T; a.rope_H = rope_H; a.rope_W = rope_W;
+  a.x_rot = x_rot; a.pooled = pooled;
+  a.tmap = nullptr;
+  a.map3 = 0;
+  pl.has_map = false;
+  // bf16/fp16 blocks of 64 d-wide halves stream through a TMA ring; the map needs mergeable batch
+  // and head strides, which the register kernel does not
+  if (dtype != BSA_DTYPE_F32 && !rope && (B == 1 || sb == static_cast<int64_t>(H) * sh)) {
+    // a map that cannot be built only selects the register kernel: keep the caller's last message
+    char saved[sizeof(g_msg)];
+    memcpy(saved, g_msg, sizeof(g_msg));
+    const int64_t st[3] = {sb, sh, ss};
+    if (make_map(&pl.map, x, dtype, B, H, D, st, T, Hl, Wl, cT, cH, cW, "x", &a.map3) == BSA_OK) pl.has_map = true;
+    else memcpy(g_msg, saved, sizeof(g_msg));
+  }
   return BSA_OK;
 }
+
+int pool_run(PoolPlan& pl, void* stream) {
+  pl.a.tmap = pl.has_map ? &pl.map : nullptr;
+  const int rc = bsa::launch_pool(pl.a, static_cast<cudaStream_t>(stream));
+  if (rc == BSA_ERR_CUDA) return cuda_fail("pool kernel launch");
+  if (rc) return fail(rc, "pool: unsupported configuration");
+  return BSA_OK;
+}
+
+struct AttnPlan {
+  CUtensorMap mq, mk, mv;
+  bsa::AttnArgs a;
+};
+
+int attn_plan(AttnPlan& pl, const void* q, const void* k, const void* v, const int32_t* block_indices, int dtype,
+              int B, int H, int S, int D, const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides,
+              int T, int Hl, int Wl, int cT, int cH, int cW, int topk, float sm_scale, void* out,
+              const int64_t* out_strides, int sm_reserve) {
+  if (sm_reserve < 0) return fail(BSA_ERR_ARG, "sm_reserve=%d must be >= 0", sm_reserve);
+  if (!q || !k || !v || !block_indices || !out || !q_strides || !k_strides || !v_strides || !out_strides)
+    return fail(BSA_ERR_ARG, "null pointer");
+  if (dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
+    return fail(BSA_ERR_DTYPE, "sparse attention supports fp16 and bf16 inputs (dtype code %d)", dtype);
+  if (B <= 0 || H <= 0 || S <= 0) return fail(BSA_ERR_SHAPE, "empty tensor");
+  int rc = check_geometry(S, T, Hl, Wl, cT, cH, cW);
+  if (rc) return rc;
+  if (cT * cH * cW != 64)
+    return fail(BSA_ERR_SHAPE, "block size must be 64 tokens (chunk_thw product), got %d", cT * cH * cW);
+  if (D % 8 || D < 8 || D > 128) return fail(BSA_ERR_SHAPE, "head_dim D=%d must be a multiple of 8 in [8, 128]", D);
+  const int nb = S / 64;
+  if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
+  if (!aligned16(block_indices)) return fail(BSA_ERR_ALIGN, "block_indices must be 16-byte aligned");
+  if ((rc = make_map(&pl.mq, q, dtype, B, H, D, q_strides, T, Hl, Wl, cT, cH, cW, "q", &pl.a.map3))) return rc;
+  if ((rc = make_map(&pl.mk, k, dtype, B, H, D, k_strides, T, Hl, Wl, cT, cH, cW, "k"))) return rc;
+  if ((rc = make_map(&pl.mv, v, dtype, B, H, D, v_strides, T, Hl, Wl, cT, cH, cW, "v"))) return rc;
+  bsa::AttnArgs& a = pl.a;  // a.map3 was set by make_map (the same form for q, k and v)
+  a.idx = block_indices; a.out = out;
+  a.B = B; a.H = H; a.S = S; a.D = D; a.nb = nb; a.topk = topk;
+  a.Hl = Hl; a.Wl = Wl; a.cT = cT; a.cH = cH; a.cW = cW;
+  a.out_sb = out_strides[0]; a.out_sh = out_strides[1]; a.out_ss = out_strides[2];
+  a.sm_scale = sm_scale;
+  a.is_bf16 = dtype == BSA_DTYPE_BF16;
+  a.sm_reserve = sm_reserve;
+  return BSA_OK;
+}
+
+int attn_run(AttnPlan& pl, void* stream) {
+  const int rc = bsa::launch_attn(&pl.mq, &pl.mk, &pl.mv, pl.a, static_cast<cudaStream_t>(stream));
+  if (rc == BSA_ERR_CUDA) return cuda_fail("attention kernel launch");
+  return rc;
+}
+
+int64_t score_ld(int nb) { return (static_cast<int64_t>(nb) + 3) & ~int64_t(3); }
 
 }  // namespace
 
@@ -139,38 +260,11 @@ int bsa_device_error(int clear) {
 int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss, int T,
                   int Hl, int Wl, int cT, int cH, int cW, const float* rope, int rope_dt, int rope_dh, int rope_dw,
                   int rope_T, int rope_H, int rope_W, void* x_rot, float* pooled, void* stream) {
-  int rc = check_pool_args(x, dtype, B, H, S, D, sb, sh, ss, T, Hl, Wl, cT, cH, cW, pooled);
+  PoolPlan pl;
+  const int rc = pool_plan(pl, x, dtype, B, H, S, D, sb, sh, ss, T, Hl, Wl, cT, cH, cW, rope, rope_dt, rope_dh,
+                           rope_dw, rope_T, rope_H, rope_W, x_rot, pooled);
   if (rc) return rc;
-  if (rope) {
-    if (!x_rot) return fail(BSA_ERR_ARG, "x_rot is required with rope tables");
-    if (!aligned16(x_rot)) return fail(BSA_ERR_ALIGN, "x_rot must be 16-byte aligned");
-    if (rope_dt + rope_dh + rope_dw != D || (rope_dt | rope_dh | rope_dw) & 1)
-      return fail(BSA_ERR_SHAPE, "rope dims (%d, %d, %d) must be even and sum to D=%d", rope_dt, rope_dh, rope_dw, D);
-    if (static_cast<long long>(rope_T) * rope_H * rope_W != S)
-      return fail(BSA_ERR_SHAPE, "rope grid (%d, %d, %d) does not cover S=%d", rope_T, rope_H, rope_W, S);
-  }
-  bsa::PoolArgs a;
-  a.x = x; a.dtype = dtype; a.B = B; a.H = H; a.S = S; a.D = D; a.sb = sb; a.sh = sh; a.ss = ss;
-  a.T = T; a.Hl = Hl; a.Wl = Wl; a.cT = cT; a.cH = cH; a.cW = cW;
-  a.rope = rope; a.rope_dt = rope_dt; a.rope_dh = rope_dh; a.rope_dw = rope_dw;
-  a.rope_T = rope_T; a.rope_H = rope_H; a.rope_W = rope_W;
-  a.x_rot = x_rot; a.pooled = pooled;
-  // bf16/fp16 blocks of 64 d-wide halves stream through a TMA ring; the map needs mergeable batch
-  // and head strides, which the register kernel does not
-  CUtensorMap m;
-  a.tmap = nullptr;
-  if (dtype != BSA_DTYPE_F32 && (B == 1 || sb == static_cast<int64_t>(H) * sh)) {
-    // a map that cannot be built only selects the register kernel: keep the caller's last message
-    char saved[sizeof(g_msg)];
-    memcpy(saved, g_msg, sizeof(g_msg));
-    const int64_t st[3] = {sb, sh, ss};
-    if (make_map(&m, x, dtype, B, H, D, st, T, Hl, Wl, cT, cH, cW, "x") == BSA_OK) a.tmap = &m;
-    else memcpy(g_msg, saved, sizeof(g_msg));
-  }
-  rc = bsa::launch_pool(a, static_cast<cudaStream_t>(stream));
-  if (rc == BSA_ERR_CUDA) return cuda_fail("pool kernel launch");
-  if (rc) return fail(rc, "pool: unsupported configuration");
-  return BSA_OK;
+  return pool_run(pl, stream);
 }
 
 int bsa_score_topk(const float* q_pooled, const float* k_pooled, int BH, int nb, int D, int topk,
@@ -230,40 +324,12 @@ int bsa_attention_indices_ex(const void* q, const void* k, const void* v, const 
                              int B, int H, int S, int D, const int64_t* q_strides, const int64_t* k_strides,
                              const int64_t* v_strides, int T, int Hl, int Wl, int cT, int cH, int cW, int topk,
                              float sm_scale, void* out, const int64_t* out_strides, int sm_reserve, void* stream) {
-  if (sm_reserve < 0) return fail(BSA_ERR_ARG, "sm_reserve=%d must be >= 0", sm_reserve);
-  if (!q || !k || !v || !block_indices || !out || !q_strides || !k_strides || !v_strides || !out_strides)
-    return fail(BSA_ERR_ARG, "null pointer");
-  if (dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
-    return fail(BSA_ERR_DTYPE, "sparse attention supports fp16 and bf16 inputs (dtype code %d)", dtype);
-  if (B <= 0 || H <= 0 || S <= 0) return fail(BSA_ERR_SHAPE, "empty tensor");
-  int rc = check_geometry(S, T, Hl, Wl, cT, cH, cW);
+  AttnPlan pl;
+  const int rc = attn_plan(pl, q, k, v, block_indices, dtype, B, H, S, D, q_strides, k_strides, v_strides, T, Hl, Wl,
+                           cT, cH, cW, topk, sm_scale, out, out_strides, sm_reserve);
   if (rc) return rc;
-  if (cT * cH * cW != 64)
-    return fail(BSA_ERR_SHAPE, "block size must be 64 tokens (chunk_thw product), got %d", cT * cH * cW);
-  if (D % 8 || D < 8 || D > 128) return fail(BSA_ERR_SHAPE, "head_dim D=%d must be a multiple of 8 in [8, 128]", D);
-  const int nb = S / 64;
-  if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
-  if (!aligned16(block_indices)) return fail(BSA_ERR_ALIGN, "block_indices must be 16-byte aligned");
-  CUtensorMap mq, mk, mv;
-  if ((rc = make_map(&mq, q, dtype, B, H, D, q_strides, T, Hl, Wl, cT, cH, cW, "q"))) return rc;
-  if ((rc = make_map(&mk, k, dtype, B, H, D, k_strides, T, Hl, Wl, cT, cH, cW, "k"))) return rc;
-  if ((rc = make_map(&mv, v, dtype, B, H, D, v_strides, T, Hl, Wl, cT, cH, cW, "v"))) return rc;
-  bsa::AttnArgs a;
-  a.idx = block_indices; a.out = out;
-  a.B = B; a.H = H; a.S = S; a.D = D; a.nb = nb; a.topk = topk;
-  a.Hl = Hl; a.Wl = Wl; a.cT = cT; a.cH = cH; a.cW = cW;
-  a.out_sb = out_strides[0]; a.out_sh = out_strides[1]; a.out_ss = out_strides[2];
-  a.sm_scale = sm_scale;
-  a.is_bf16 = dtype == BSA_DTYPE_BF16;
-  a.sm_reserve = sm_reserve;
-  rc = bsa::launch_attn(&mq, &mk, &mv, a, static_cast<cudaStream_t>(stream));
-  if (rc == BSA_ERR_CUDA) return cuda_fail("attention kernel launch");
-  return rc;
+  return attn_run(pl, stream);
 }
-
-namespace {
-int64_t score_ld(int nb) { return (static_cast<int64_t>(nb) + 3) & ~int64_t(3); }
-}  // namespace
 
 int64_t bsa_forward_scratch_bytes(int B, int H, int S, int D, int cT, int cH, int cW) {
   const int n = cT * cH * cW;
@@ -288,44 +354,52 @@ int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B
                    int rope_dh, int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot,
                    void* scratch, int32_t* block_indices, void* out, const int64_t* out_strides, int sm_reserve,
                    void* stream) {
+  // ---- every check first: nothing is queued unless the whole call is valid
   if (sm_reserve < 0) return fail(BSA_ERR_ARG, "sm_reserve=%d must be >= 0", sm_reserve);
-  if (!scratch || !q_strides || !k_strides || !v_strides) return fail(BSA_ERR_ARG, "null pointer");
+  if (!q || !k || !v || !scratch || !block_indices || !out || !q_strides || !k_strides || !v_strides || !out_strides)
+    return fail(BSA_ERR_ARG, "null pointer");
   if (!aligned16(scratch)) return fail(BSA_ERR_ALIGN, "scratch must be 16-byte aligned");
   if (dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
     return fail(BSA_ERR_DTYPE, "sparse attention supports fp16 and bf16 inputs (dtype code %d)", dtype);
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(BSA_ERR_SHAPE, "empty tensor");
+  int rc = check_geometry(S, T, Hl, Wl, cT, cH, cW);
+  if (rc) return rc;
   const int n = cT * cH * cW;
-  if (n != 64) {
-    int rc = check_geometry(S, T, Hl, Wl, cT, cH, cW);
-    if (rc) return rc;
-    return fail(BSA_ERR_SHAPE, "block size must be 64 tokens (chunk_thw product), got %d", n);
-  }
+  if (n != 64) return fail(BSA_ERR_SHAPE, "block size must be 64 tokens (chunk_thw product), got %d", n);
   const int nb = S / 64;
+  if (D % 8 || D > 128) return fail(BSA_ERR_SHAPE, "head_dim D=%d must be a multiple of 8 in [8, 128]", D);
+  if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
   float* qp = static_cast<float*>(scratch);
   float* kp = qp + static_cast<int64_t>(B) * H * nb * D;
-  int rc = bsa_mean_pool(q, dtype, B, H, S, D, q_strides[0], q_strides[1], q_strides[2], T, Hl, Wl, cT, cH, cW, rope,
-                         rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, q_rot, qp, stream);
-  if (rc) return rc;
-  rc = bsa_mean_pool(k, dtype, B, H, S, D, k_strides[0], k_strides[1], k_strides[2], T, Hl, Wl, cT, cH, cW, rope,
-                     rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, k_rot, kp, stream);
-  if (rc) return rc;
-  {
-    if (D % 8) return fail(BSA_ERR_SHAPE, "head_dim D=%d must be a multiple of 8", D);
-    if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
-    bsa::ScoreArgs a;
-    a.qp = qp; a.kp = kp; a.BH = B * H; a.nq = nb; a.nk = nb; a.D = D; a.topk = topk;
-    a.idx = block_indices; a.ldc = static_cast<int>(score_ld(nb));
-    a.scores = kp + static_cast<int64_t>(B) * H * nb * D;
-    rc = bsa::launch_score_topk(a, static_cast<cudaStream_t>(stream));
-    if (rc == BSA_ERR_CUDA) return cuda_fail("score/top-k kernel launch");
-    if (rc) return fail(rc, "score/top-k: unsupported sizes (nb=%d)", nb);
-  }
+  PoolPlan pq, pk;
+  if ((rc = pool_plan(pq, q, dtype, B, H, S, D, q_strides[0], q_strides[1], q_strides[2], T, Hl, Wl, cT, cH, cW, rope,
+                      rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, q_rot, qp)))
+    return rc;
+  if ((rc = pool_plan(pk, k, dtype, B, H, S, D, k_strides[0], k_strides[1], k_strides[2], T, Hl, Wl, cT, cH, cW, rope,
+                      rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, k_rot, kp)))
+    return rc;
+  bsa::ScoreArgs sa;
+  sa.qp = qp; sa.kp = kp; sa.BH = B * H; sa.nq = nb; sa.nk = nb; sa.D = D; sa.topk = topk;
+  sa.idx = block_indices; sa.ldc = static_cast<int>(score_ld(nb));
+  sa.scores = kp + static_cast<int64_t>(B) * H * nb * D;
+  AttnPlan pa;
   if (rope) {
+    // the attention reads the rotated tensors the pool kernels write (contiguous [B,H,S,D])
     const int64_t cst[3] = {static_cast<int64_t>(H) * S * D, static_cast<int64_t>(S) * D, D};
-    return bsa_attention_indices_ex(q_rot, k_rot, v, block_indices, dtype, B, H, S, D, cst, cst, v_strides, T, Hl,
-                                    Wl, cT, cH, cW, topk, sm_scale, out, out_strides, sm_reserve, stream);
+    rc = attn_plan(pa, q_rot, k_rot, v, block_indices, dtype, B, H, S, D, cst, cst, v_strides, T, Hl, Wl, cT, cH, cW,
+                   topk, sm_scale, out, out_strides, sm_reserve);
+  } else {
+    rc = attn_plan(pa, q, k, v, block_indices, dtype, B, H, S, D, q_strides, k_strides, v_strides, T, Hl, Wl, cT, cH,
+                   cW, topk, sm_scale, out, out_strides, sm_reserve);
   }
-  return bsa_attention_indices_ex(q, k, v, block_indices, dtype, B, H, S, D, q_strides, k_strides, v_strides, T, Hl,
-                                  Wl, cT, cH, cW, topk, sm_scale, out, out_strides, sm_reserve, stream);
+  if (rc) return rc;
+  // ---- launches
+  if ((rc = pool_run(pq, stream))) return rc;
+  if ((rc = pool_run(pk, stream))) return rc;
+  rc = bsa::launch_score_topk(sa, static_cast<cudaStream_t>(stream));
+  if (rc == BSA_ERR_CUDA) return cuda_fail("score/top-k kernel launch");
+  if (rc) return fail(rc, "score/top-k: unsupported sizes (nb=%d)", nb);
+  return attn_run(pa, stream);
 }
 
 }  // extern "C"

@@ -20,7 +20,8 @@ struct PoolArgs {
   int rope_T, rope_H, rope_W;  // RoPE grid; token s sits at (s / (H*W), (s / W) % H, s % W)
   void* x_rot;           // [B,H,S,D] contiguous, same dtype as x (required when rope != null)
   float* pooled;         // [B*H, nb, D] fp32
-  const CUtensorMap* tmap;  // nullable: 5-D block map over x (bf16/fp16); selects the TMA-ring kernel
+  const CUtensorMap* tmap;  // nullable: block map over x (bf16/fp16); selects the TMA-ring kernel
+  int map3;                 // tmap is 3-D (d, s, b*h) (contiguous blocks), else 5-D (d, w, h, t, b*h)
 };
 int launch_pool(const PoolArgs& a, cudaStream_t stream);
 
@@ -47,6 +48,7 @@ struct AttnArgs {
   float sm_scale;
   int is_bf16;
   int sm_reserve;  // SMs left free for concurrent kernels (the persistent grid covers the rest)
+  int map3;        // the tensor maps are 3-D (d, s, b*h): blocks are contiguous 64-token runs
 };
 int launch_attn(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v, const AttnArgs& a,
                 cudaStream_t stream);

@@ -4,12 +4,17 @@
 // attention: code inside a region whose memory must be fixed in advance, embedders that own the
 // whole device budget and forbid allocations from libraries, or hosts that bind this library
 // without a device allocator of their own.  bsa_forward needs scratch for the pooled fp32 Q/K
-// blocks, which its caller normally passes in.  This variant takes that scratch from a fixed array
-// compiled into the library instead, so the caller only passes inputs and outputs.
+// blocks and the fp32 block-score matrix, which its caller normally passes in.  This variant takes
+// that scratch from a fixed array compiled into the library instead, so the caller only passes
+// inputs and outputs.
 //
 // The array is a file-scope __device__ allocation of BSA_NOALLOC_SCRATCH_BYTES (16 MiB): every GPU
 // that loads the library holds it until the process exits.  Requests that need more scratch
 // (bsa_forward_scratch_bytes > 16 MiB) are rejected with BSA_ERR_SHAPE and a message.
+//
+// The array's device address is resolved once per device and cached for the life of the process.
+// A device reset (cudaDeviceReset) is not supported: it reloads the module, and the cached address
+// would then be stale.
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -35,11 +40,15 @@ extern "C" int bsa_forward_noalloc(const void* q, const void* k, const void* v, 
                                    const float* rope, int rope_dt, int rope_dh, int rope_dw, int rope_T,
                                    int rope_H, int rope_W, void* q_rot, void* k_rot, int32_t* block_indices,
                                    void* out, const int64_t* out_strides, void* stream) {
+  // outputs are checked before the device is touched, so a rejected call has done nothing
+  if (!q || !k || !v || !block_indices || !out || !q_strides || !k_strides || !v_strides || !out_strides)
+    return bsa::set_error(BSA_ERR_ARG, "bsa_forward_noalloc: null pointer");
   const int64_t need = bsa_forward_scratch_bytes(B, H, S, D, cT, cH, cW);
   if (need > static_cast<int64_t>(kScratchBytes))
     return bsa::set_error(BSA_ERR_SHAPE,
-                          "bsa_forward_noalloc: this call needs %lld bytes of scratch (pooled Q/K), above the "
-                          "library's fixed %zu-byte array; use bsa_forward with caller-provided scratch",
+                          "bsa_forward_noalloc: this call needs %lld bytes of scratch (pooled Q/K and score "
+                          "matrix), above the library's fixed %zu-byte array; use bsa_forward with "
+                          "caller-provided scratch",
                           static_cast<long long>(need), kScratchBytes);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)

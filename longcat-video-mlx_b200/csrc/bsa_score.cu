@@ -16,6 +16,7 @@
 // back one row per warp.
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 #include <type_traits>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -42,6 +43,7 @@ struct Geo {
   int Hl, Wl, cT, cH, cW, Bh, Bw;
   const float* rope;
   int rdt, rdh, rdw, rT, rH, rW;
+  int map3;  // the TMA-ring kernel's map is 3-D (d, s, b*h): blocks are contiguous token runs
 };
 
 // Four consecutive d values of one token row: 8 bytes (fp16/bf16) or 16 bytes (fp32).
@@ -222,9 +224,16 @@ __global__ void __launch_bounds__(kThreads, kRope ? 3 : 4)
 // The same pooling (without RoPE) for bf16/fp16 inputs, with the blocks streamed into shared memory by
 // TMA: one producer lane keeps up to kRing blocks (16 KB each) in flight per SM, and kConsumers warps
 // reduce them.  Row order and the fp32 pairwise tree are those of pool_kernel, so results are identical.
-constexpr int kConsumers = 8;
+//
+// Consumer warp c takes the CTA's blocks c, c + kConsumers, ... and owns slots 2c and 2c + 1, which it
+// uses alternately: every full/empty phase of a slot is then produced and consumed in order by one
+// producer and one consumer.  (Round-robin blocks over a shared ring let a consumer reach its wait
+// before the slot's previous block had landed -- TMA loads may complete out of issue order -- and a
+// parity wait one phase ahead of its barrier reads the phase before as complete.)
+constexpr int kConsumers = 6;
+constexpr int kSlotsPerConsumer = 2;
 constexpr int kTmaThreads = 32 * (kConsumers + 1);
-constexpr int kRing = 12;
+constexpr int kRing = kConsumers * kSlotsPerConsumer;
 constexpr int kSlotBytes = 16384;  // two 8 KB d-halves of up to 64 rows x 128 B, 128B-swizzled
 struct RingSmem {
   uint64_t full[kRing];
@@ -280,9 +289,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       prefetch_tmap(&tm);
       int i = 0;
       for (; i < cnt; ++i) {
-        const int slot = i % kRing;
-        if (i >= kRing &&
-            !mbar_wait(&rs.empty[slot], static_cast<uint32_t>((i / kRing - 1) & 1), abort_flag, &g_score_err, 301))
+        // block i -> consumer i % kConsumers, its (i / kConsumers)-th block, slot 2c + (m & 1), fill m / 2
+        const int m = i / kConsumers;
+        const int slot = (i - m * kConsumers) * kSlotsPerConsumer + (m & 1);
+        const int fill = m >> 1;
+        if (fill >= 1 &&
+            !mbar_wait(&rs.empty[slot], static_cast<uint32_t>((fill - 1) & 1), abort_flag, &g_score_err, 301))
           break;
         const int item = static_cast<int>(blockIdx.x) + i * G;
         const int blk = item % g.nb;
@@ -293,25 +305,35 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
         const int bw = rr - bhh * g.Bw;
         uint8_t* dst = ring + slot * kSlotBytes;
         mbar_arrive_expect_tx(&rs.full[slot], 2u * box_bytes);
-        tma_load_5d(dst, &tm, &rs.full[slot], 0, bw * g.cW, bhh * g.cH, bt * g.cT, bh);
-        tma_load_5d(dst + 8192, &tm, &rs.full[slot], 64, bw * g.cW, bhh * g.cH, bt * g.cT, bh);
+        if (g.map3) {  // contiguous blocks: token blk * n of the (d, s, b*h) map
+          tma_load_3d(dst, &tm, &rs.full[slot], 0, blk * g.n, bh);
+          tma_load_3d(dst + 8192, &tm, &rs.full[slot], 64, blk * g.n, bh);
+        } else {
+          tma_load_5d(dst, &tm, &rs.full[slot], 0, bw * g.cW, bhh * g.cH, bt * g.cT, bh);
+          tma_load_5d(dst + 8192, &tm, &rs.full[slot], 64, bw * g.cW, bhh * g.cH, bt * g.cT, bh);
+        }
       }
-      // teardown: no TMA write into this CTA's shared memory may still be in flight
+      // teardown: no TMA write into this CTA's shared memory may still be in flight.  The last block
+      // issued into each slot is its latest fill; its phase is the newest one of that barrier.
       const uint64_t t0 = globaltimer_ns();
-      for (int j = (i > kRing ? i - kRing : 0); j < i; ++j)
-        while (!mbar_try_wait(&rs.full[j % kRing], static_cast<uint32_t>((j / kRing) & 1)) &&
+      for (int j = (i > kRing ? i - kRing : 0); j < i; ++j) {
+        const int m = j / kConsumers;
+        const int slot = (j - m * kConsumers) * kSlotsPerConsumer + (m & 1);
+        while (!mbar_try_wait(&rs.full[slot], static_cast<uint32_t>((m >> 1) & 1)) &&
                globaltimer_ns() - t0 < kWaitLimitNs) {
         }
+      }
     }
     __syncwarp();
   } else {
-    // ---------------------------------------------------------------- consumers: warp w takes blocks w, w+8, ...
+    // ---------------------------------------------------------------- consumers: warp c takes blocks c, c+6, ...
     const int d0 = lane * 4;
     const bool dact = d0 < g.D;
     const float inv_n = 1.0f / static_cast<float>(g.n);
-    for (int i = warp; i < cnt; i += kConsumers) {
-      const int slot = i % kRing;
-      bool ok = mbar_wait(&rs.full[slot], static_cast<uint32_t>((i / kRing) & 1), abort_flag, &g_score_err, 302);
+    int m = 0;  // this warp's blocks so far
+    for (int i = warp; i < cnt; i += kConsumers, ++m) {
+      const int slot = warp * kSlotsPerConsumer + (m & 1);
+      bool ok = mbar_wait(&rs.full[slot], static_cast<uint32_t>((m >> 1) & 1), abort_flag, &g_score_err, 302);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const uint8_t* sl = ring + slot * kSlotBytes;
@@ -394,6 +416,7 @@ int launch_pool(const PoolArgs& a, cudaStream_t stream) {
   g.Bh = a.Hl / a.cH; g.Bw = a.Wl / a.cW;
   g.rope = a.rope; g.rdt = a.rope_dt; g.rdh = a.rope_dh; g.rdw = a.rope_dw;
   g.rT = a.rope_T; g.rH = a.rope_H; g.rW = a.rope_W;
+  g.map3 = a.map3;
   if (n < 1 || n > 64 || (n & (n - 1)) || a.D > 128 || a.D % 4) return BSA_ERR_SHAPE;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
@@ -408,16 +431,21 @@ int launch_pool(const PoolArgs& a, cudaStream_t stream) {
   if (a.tmap && !rope && (a.dtype == BSA_DTYPE_BF16 || a.dtype == BSA_DTYPE_F16)) {
     // TMA ring: one persistent CTA per SM.  With fused RoPE the register kernel stays faster (its 32
     // warps per SM hide the per-row table loads and the rotated-row stores; 1.77 vs 2.22 ms of routing)
+    // the shared-memory opt-in is per device; first calls from several host threads may race here
+    static std::mutex mu;
     static bool configured[64][2] = {};
     const int ti = a.dtype == BSA_DTYPE_BF16 ? 0 : 1;
-    if (dev < 64 && !configured[dev][ti]) {
-      const cudaError_t e =
-          ti == 0 ? cudaFuncSetAttribute(pool_tma_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kTmaSmemBytes)
-                  : cudaFuncSetAttribute(pool_tma_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kTmaSmemBytes);
-      if (e != cudaSuccess) return BSA_ERR_CUDA;
-      configured[dev][ti] = true;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (dev >= 64 || !configured[dev][ti]) {
+        const cudaError_t e =
+            ti == 0 ? cudaFuncSetAttribute(pool_tma_kernel<__nv_bfloat16>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmemBytes)
+                    : cudaFuncSetAttribute(pool_tma_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kTmaSmemBytes);
+        if (e != cudaSuccess) return BSA_ERR_CUDA;
+        if (dev < 64) configured[dev][ti] = true;
+      }
     }
     const dim3 tgd(static_cast<unsigned>(total < sms ? total : sms), 1, 1);
     if (ti == 0) pool_tma_kernel<__nv_bfloat16><<<tgd, kTmaThreads, kTmaSmemBytes, stream>>>(*a.tmap, a.pooled, g);
@@ -547,9 +575,11 @@ __global__ void __launch_bounds__(kThreads, 2) score_gemm_kernel(Args a) {
 }  // namespace gemm
 
 // ======================================================================== top-k per row
-// One warp per score row.  The k-th largest key T is found by a binary search over the 32-bit
-// order-preserving keys (warp-wide counts, no shared-memory atomics); the row is then scanned in
-// ascending block order taking every key above T and the first `need` keys equal to T.
+// One warp per score row.  The k-th largest key T is found over 32-bit order-preserving keys: by a
+// radix select (8-bit digits counted in a per-warp shared histogram) for rows that fit in registers
+// (up to 3,072 keys), by a binary search over the key range for longer rows, which are re-read
+// from memory.  The row is then scanned in ascending block order taking every key above T and the
+// first `need` keys equal to T.
 namespace topk {
 constexpr int kThreads = 256;
 

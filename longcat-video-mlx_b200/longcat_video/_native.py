@@ -67,6 +67,12 @@ class BSAError(RuntimeError):
     """A CUDA-side failure of the BSA engine (launch error, device error flag)."""
 
 
+class BSAShapeError(ValueError):
+    """The latent shape is not a multiple of ``chunk_thw`` or does not match S
+    (``block_sparse_attention.py:86-96``).  This is the one ``ValueError`` the DiT hook turns into
+    dense attention (``attention.py:174-179``); every other engine error reaches the caller."""
+
+
 def library_loaded() -> bool:
     return _lib is not None
 
@@ -131,13 +137,31 @@ def _strides(t: torch.Tensor):
 
 
 def _merge_batch(t: torch.Tensor) -> torch.Tensor:
-    """The attention kernel reads q/k/v through one 5-D TMA map whose last axis is b*H + h, so for B > 1
-    the batch stride must equal H times the head stride.  Views that break this (the DiT's
-    ``reshape(B, N, 3, H, D).permute(2, 0, 3, 1, 4)`` at B > 1) are copied once to a contiguous layout;
-    everything else is used in place."""
-    if t.dim() == 4 and t.shape[0] > 1 and t.stride(0) != t.shape[1] * t.stride(1):
+    """A view the kernels can read in place, else a one-time contiguous copy.
+
+    The kernels read q/k/v through TMA maps: the base address and every stride must be multiples of
+    16 bytes, and the last axis of the attention map is b*H + h, so for B > 1 the batch stride must
+    equal H times the head stride.  Views that break either rule (the DiT's
+    ``reshape(B, N, 3, H, D).permute(2, 0, 3, 1, 4)`` at B > 1, a narrowed or offset view) are copied
+    once to a contiguous layout; everything else is used in place."""
+    if t.dim() != 4:
+        return t
+    if _misaligned(t):
+        return t.clone(memory_format=torch.contiguous_format)  # a fresh, aligned allocation
+    if t.shape[0] > 1 and t.stride(0) != t.shape[1] * t.stride(1):
         return t.contiguous()
     return t
+
+
+def _misaligned(t: torch.Tensor) -> bool:
+    e = t.element_size()
+    return bool(t.data_ptr() % 16 or any((t.stride(i) * e) % 16 for i in range(t.dim() - 1) if t.shape[i] > 1))
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    """The pooling kernels accept any batch and head strides but need a 16-byte aligned base and
+    16-byte multiple strides; other views are copied once to a contiguous layout."""
+    return t.clone(memory_format=torch.contiguous_format) if t.dim() == 4 and _misaligned(t) else t
 
 
 def _dtype_code(t: torch.Tensor) -> int:
@@ -151,11 +175,11 @@ def _geometry(S: int, shape: Sequence[int], chunk_thw: Sequence[int]):
     T, H_, W = (int(v) for v in shape)
     cT, cH, cW = (int(v) for v in chunk_thw)
     if T % cT or H_ % cH or W % cW:
-        raise ValueError(
+        raise BSAShapeError(
             f"Latent shape ({T}, {H_}, {W}) must be a multiple of "
             f"chunk_thw {tuple(chunk_thw)}; refinement padding should guarantee this.")
     if S != T * H_ * W:
-        raise ValueError(f"S={S} doesn't match T*H*W={T * H_ * W} for shape {tuple(shape)}")
+        raise BSAShapeError(f"S={S} doesn't match T*H*W={T * H_ * W} for shape {tuple(shape)}")
     return T, H_, W, cT, cH, cW
 
 
@@ -168,6 +192,7 @@ def mean_pool(x: torch.Tensor, shape, chunk_thw, rope: Optional[Tuple] = None) -
     B, H, S, D = x.shape
     T, H_, W, cT, cH, cW = _geometry(S, shape, chunk_thw)
     nb = S // (cT * cH * cW)
+    x = _aligned(x)
     pooled = torch.empty((B, H, nb, D), device=x.device, dtype=torch.float32)
     st = _strides(x)
     x_rot = None

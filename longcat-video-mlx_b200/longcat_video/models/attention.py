@@ -4,8 +4,8 @@
 Only what the BSA path needs is here: QKV projection, fp32 RMSNorm on q/k (blocks.py:55-73),
 3-D RoPE, ``_process_attn`` (the hook, :71-179) and the output projection.  Every BSA backend
 name the reference accepts routes to the one CUDA engine; the hook's own fallback -- a
-``ValueError`` from BSA (shape not a multiple of chunk_thw) falls back to dense attention
-(:174-179) -- is kept as the reference has it.  With BSA on, RoPE is fused into the routing
+shape that is not a multiple of chunk_thw falls back to dense attention (:174-179) -- is kept as
+the reference has it, and only for that error.  With BSA on, RoPE is fused into the routing
 kernel instead of being applied as a separate pass.
 """
 
@@ -16,6 +16,7 @@ from typing import Optional, Tuple
 import torch
 import torch.nn.functional as F
 
+from .._native import BSAShapeError
 from .block_sparse_attention import bsa_attention
 from .rope_3d import RotaryPositionalEmbedding
 
@@ -69,9 +70,12 @@ class Attention(torch.nn.Module):
                 return bsa_attention(q, k, v, shape=shape, sparsity=self.bsa_sparsity,
                                      chunk_thw=self.bsa_chunk_thw, sm_scale=self.scale, topk=self.bsa_topk,
                                      rope=rope)
-            except ValueError:
-                # shape not a multiple of chunk_thw (or outside the kernel's limits): the
-                # reference falls back to dense attention here (attention.py:174-179)
+            except BSAShapeError:
+                # shape not a multiple of chunk_thw: the reference falls back to dense attention
+                # here (attention.py:174-179).  Every other engine error (unsupported head_dim or
+                # dtype) propagates: a silent dense fallback would cost 1/(1 - sparsity) times the
+                # FLOPs with no message.  Views the kernels cannot read in place are copied once by
+                # the engine's host layer, not refused.
                 pass
         if rope_grid is not None:
             q, k = self.rope_3d(q, k, rope_grid)

@@ -35,8 +35,13 @@ class AliasError(AssertionError):
 
 
 def wait(bar, phase):
-    """A role waits for `phase` of `bar` to complete.  Returns True when it may proceed."""
-    if bar.completed >= phase + 2:
+    """A role waits for `phase` of `bar` to complete.  Returns True when it may proceed.
+
+    The hardware wait sees only the parity of the barrier's current phase, so it reads correctly only
+    while the barrier has completed `phase` or `phase + 1` phases.  Two more (the barrier ran a whole
+    phase past the waiter) or one fewer (the waiter is a phase ahead: the previous phase of the same
+    parity would read as complete) are both misreads."""
+    if bar.completed >= phase + 2 or bar.completed < phase:
         raise AliasError(f"{bar.name}: waiter for phase {phase} sees {bar.completed} completed phases")
     return bar.completed == phase + 1
 
@@ -64,8 +69,10 @@ def run_protocol(units, nsteps, kstages, vslots, qbufs, seed, rescale_prob=0.2):
         bar(("ep", q), 2)
     bar(("o_empty",), 8)
 
-    # asynchronous completions: per issuing thread, a FIFO of barrier names completing in order
+    # asynchronous completions, per issuing thread: tcgen05.commit arrivals complete in issue order
+    # (a commit tracks every earlier MMA of its thread); TMA loads may complete in any order
     async_q = {"tma_k": [], "tma_v": [], "tma_q": [], "mma_qk": [], "mma_pv": []}
+    in_order = {"mma_qk", "mma_pv"}
 
     hs = ((nsteps + 1) // 2, nsteps // 2)
 
@@ -172,16 +179,17 @@ def run_protocol(units, nsteps, kstages, vslots, qbufs, seed, rescale_prob=0.2):
                     yield
                 if n + 1 < units:
                     yield from copy_q(n + 1)
-            l0 = (n + 1) * hs[0] - 1
-            while not wait(B[("p_empty", 0, l0 & 1)], l0 >> 1):
-                yield
-            if two_halves:
-                l1 = (n + 1) * hs[1] - 1
-                while not wait(B[("p_empty", 1, l1 & 1)], l1 >> 1):
+            if active:  # this half's last PV of the unit; the ep handshake carries the other half's
+                last = i - 1
+                while not wait(B[("p_empty", h, last & 1)], last >> 1):
                     yield
             B[("ep", qq)].arrive()
             while not wait(B[("ep", qq)], n):
                 yield
+            # O is read here: every PV of this unit, in both halves, must have completed
+            for hh in ((0, 1) if two_halves else (0,)):
+                lh = (n + 1) * hs[hh] - 1
+                assert B[("p_empty", hh, lh & 1)].completed >= (lh >> 1) + 1, ("O read early", n, hh)
             B[("o_empty",)].arrive()
             yield
 
@@ -193,7 +201,7 @@ def run_protocol(units, nsteps, kstages, vslots, qbufs, seed, rescale_prob=0.2):
         pending = [k for k, v in async_q.items() if v]
         if pending and (not live or rng.random() < 0.35):
             k = rng.choice(pending)
-            B[async_q[k].pop(0)].arrive()
+            B[async_q[k].pop(0 if k in in_order else rng.randrange(len(async_q[k])))].arrive()
             stalls = 0
             continue
         r = rng.choice(live)
@@ -221,8 +229,80 @@ def test_attention_barrier_protocol(nsteps, units, rings):
 
 
 def test_protocol_model_detects_aliasing():
-    """The checker is live: a waiter that lags its barrier by two phases is reported."""
+    """The checker is live: a waiter that lags its barrier by two phases, or runs a phase ahead of it,
+    is reported."""
     b = Barrier("x", 1)
     b.arrive(); b.arrive()
     with pytest.raises(AliasError):
         wait(b, 0)
+    with pytest.raises(AliasError):
+        wait(Barrier("y", 1), 1)
+
+
+# ------------------------------------------------------------------ the pooling kernel's TMA ring
+def run_pool_ring(cnt, consumers, ring, owned, seed, p_land=0.1):
+    """csrc/bsa_score.cu pool_tma_kernel: one producer lane streams `cnt` blocks into `ring` slots; each
+    block is reduced by one of `consumers` warps.  owned=True is the kernel's layout (consumer c takes
+    blocks c, c + consumers, ... into its own two slots); owned=False is a shared ring with round-robin
+    blocks.  TMA loads complete in any order."""
+    rng = random.Random(seed)
+    full = [Barrier(("full", s), 1) for s in range(ring)]
+    empty = [Barrier(("empty", s), 1) for s in range(ring)]
+    per = ring // consumers
+
+    def place(i):
+        if owned:
+            m = i // consumers
+            return (i % consumers) * per + (m % per), m // per
+        return i % ring, i // ring
+
+    tma = []
+
+    def producer():
+        for i in range(cnt):
+            slot, fill = place(i)
+            if fill >= 1:
+                while not wait(empty[slot], fill - 1):
+                    yield
+            tma.append(slot)
+            yield
+
+    def consumer(c):
+        for i in range(c, cnt, consumers):
+            slot, fill = place(i)
+            while not wait(full[slot], fill):
+                yield
+            yield  # rows read into registers
+            empty[slot].arrive()
+
+    roles = [producer()] + [consumer(c) for c in range(consumers)]
+    live = list(range(len(roles)))
+    stalls = 0
+    while live or tma:
+        if tma and (not live or rng.random() < p_land):
+            full[tma.pop(rng.randrange(len(tma)))].arrive()
+            continue
+        r = rng.choice(live)
+        try:
+            next(roles[r])
+            stalls += 1
+        except StopIteration:
+            live.remove(r)
+            stalls = 0
+        if stalls > 200000:
+            raise AssertionError("deadlock")
+    assert all(b.pending == 0 for b in full + empty)
+
+
+@pytest.mark.parametrize("cnt", [1, 5, 12, 13, 97, 292])
+def test_pool_ring_protocol(cnt):
+    for seed in range(8):
+        run_pool_ring(cnt, consumers=6, ring=12, owned=True, seed=seed)
+
+
+def test_pool_ring_model_rejects_shared_round_robin_ring():
+    """The layout the kernel replaced (8 warps round-robin over a shared 12-slot ring) lets a consumer
+    wait on a slot whose previous block has not landed yet; the model reports it."""
+    with pytest.raises(AliasError):
+        for seed in range(50):
+            run_pool_ring(292, consumers=8, ring=12, owned=False, seed=seed)

@@ -61,3 +61,46 @@ def test_forward_scratch_size(lib):
     f.argtypes = [ctypes.c_int] * 7
     # pooled Q and K (2 x B*H x nb x D fp32) + the score matrix (B*H x nb x nb rounded to 4) at config 2
     assert f(1, 32, 86400, 128, 1, 1, 64) == 2 * 32 * 1350 * 128 * 4 + 32 * 1350 * 1352 * 4
+
+
+def _forward_args(lib, name):
+    i64p = ctypes.POINTER(ctypes.c_int64)
+    vp, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    fn = getattr(lib, name)
+    head = [vp, vp, vp, i, i, i, i, i, i64p, i64p, i64p, i, i, i, i, i, i, i, f, vp, i, i, i, i, i, i, vp, vp]
+    fn.argtypes = head + ([vp] if name == "bsa_forward" else []) + [vp, vp, i64p, vp]
+    fn.restype = i
+    return fn
+
+
+@pytest.mark.parametrize("name", ["bsa_forward", "bsa_forward_noalloc"])
+@pytest.mark.parametrize("missing", ["block_indices", "out", "out_strides"])
+def test_forward_rejects_null_outputs_before_any_launch(lib, name, missing):
+    """A null output is refused on the host with BSA_ERR_ARG.  The checks run before the first CUDA call,
+    so the pointers below (never dereferenced) and the absent GPU are never touched."""
+    fn = _forward_args(lib, name)
+    fake = 1 << 20  # 16-byte aligned, never dereferenced
+    st = (ctypes.c_int64 * 3)(64 * 128, 64 * 128, 128)
+    B, H, S, D = 1, 1, 64, 128
+    idx = None if missing == "block_indices" else fake
+    out = None if missing == "out" else fake
+    ost = None if missing == "out_strides" else st
+    args = [fake, fake, fake, 2, B, H, S, D, st, st, st, 1, 1, 64, 1, 1, 64, 1, 0.088, None, 0, 0, 0, 0, 0, 0, None,
+            None]
+    if name == "bsa_forward":
+        args.append(fake)  # scratch
+    args += [idx, out, ost, None]
+    assert fn(*args) == 7  # BSA_ERR_ARG
+    buf = ctypes.create_string_buffer(256)
+    lib.bsa_last_error(buf, 256)
+    assert b"null" in buf.value
+
+
+def test_forward_rejects_bad_topk_before_any_launch(lib):
+    fn = _forward_args(lib, "bsa_forward")
+    fake = 1 << 20
+    st = (ctypes.c_int64 * 3)(64 * 128, 64 * 128, 128)
+    for topk in (0, 2):  # one 64-token block: topk must be 1
+        rc = fn(fake, fake, fake, 2, 1, 1, 64, 128, st, st, st, 1, 1, 64, 1, 1, 64, topk, 0.088, None, 0, 0, 0, 0, 0, 0,
+                None, None, fake, fake, fake, st, None)
+        assert rc == 1  # BSA_ERR_SHAPE

@@ -137,8 +137,7 @@ def _random_indices(B, H, nb, k, seed):
 def test_attention_indices_vs_oracle(cuda, dtype, D, k):
     from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
 
-    shape, chunk = (4, 8, 8), (4, 4, 4)  # 4 blocks... use a larger grid for k up to 8
-    shape = (8, 8, 8)
+    shape, chunk = (8, 8, 8), (4, 4, 4)  # 8 voxel blocks, so k up to 8
     B, H, S = 1, 2, 512
     nb = S // 64
     q = _rand((B, H, S, D), dtype, 10 + D, cuda)
@@ -387,3 +386,74 @@ def test_host_tensors_stream_through_gpu(cuda, B, H, group):
     assert host_out.device.type == "cpu" and host_idx.device.type == "cpu"
     assert torch.equal(host_idx, dev_idx.cpu())
     assert torch.equal(host_out, dev_out.cpu())
+
+
+# ------------------------------------------------------------------ the benchmark shapes at full size
+@pytest.mark.parametrize("name", ["config3_s0.875", "config3_s0.75"])
+def test_forward_config3_fp16_sparsity_sweep(cuda, name):
+    """Config 3 at k = 169 and k = 338 (fp16, i.i.d. inputs, near-tied pooled scores): routing exact on
+    every q block of two heads, outputs on sampled q blocks."""
+    from longcat_video.workloads import CONFIGS, make_qkv
+
+    cfg = CONFIGS[name]
+    q, k, v = make_qkv(cfg, cuda, seed=2, heads=2)
+    _full_forward_check(q, k, v, cfg.shape, cfg.chunk, cfg.topk, qblocks=[0, 1, 500, 1348, 1349])
+
+
+def test_forward_config4_fused_rope_fullsize(cuda):
+    """Config 4: pre-RoPE Q/K with the 3-D RoPE of the real 24x45x80 latent grid fused into routing.
+    The rotated bytes equal the oracle's, routing is exact on two heads, outputs on sampled q blocks."""
+    from longcat_video import _native
+    from longcat_video.models.rope_3d import RopeTables
+    from longcat_video.workloads import CONFIGS, make_qkv
+
+    cfg = CONFIGS["config4"]
+    q, k, v = make_qkv(cfg, cuda, seed=3, heads=2)
+    rope = RopeTables(cfg.grid, cfg.D, cuda)
+    _, q_rot = _native.mean_pool(q, cfg.shape, cfg.chunk, rope=rope.native_args())
+    cos, sin = orc.rope_full_tables(cfg.grid, cfg.D)
+    rows = np.r_[0:256, 40000:40256, cfg.S - 256:cfg.S]  # first, middle and last tokens of every head
+    ref_rot = orc.apply_rope(_np(q[:, :, rows]), cos[rows], sin[rows], "bf16")
+    assert _np(q_rot[:, :, rows]).tobytes() == ref_rot.tobytes()
+    _full_forward_check(q, k, v, cfg.shape, cfg.chunk, cfg.topk, qblocks=[0, 700, 1349], rope=rope)
+
+
+def test_forward_config5_fullsize(cuda):
+    """Config 5 (S = 172,800, 2,700 blocks, top-169): rows of 2,700 keys take the 96-keys-per-lane
+    selection, and every unit runs 85 two-block steps.  Routing exact on two heads."""
+    from longcat_video.workloads import CONFIGS, make_qkv
+
+    cfg = CONFIGS["config5"]
+    q, k, v = make_qkv(cfg, cuda, seed=4, heads=2)
+    _full_forward_check(q, k, v, cfg.shape, cfg.chunk, cfg.topk, qblocks=[0, 1351, 2699])
+
+
+@pytest.mark.parametrize("k", [1, 2, 3])
+def test_attention_many_units_per_cta(cuda, k):
+    """608 (head, q-block) units on 148 persistent CTAs: every CTA runs four or five units back to back.
+    With k = 1 or 2 there is one two-block step per unit, so lane half 1 of the kernel stays idle while
+    the unit loop, the Q buffers and the epilogue hand-offs cycle."""
+    from longcat_video.models.block_sparse_attention_cuda import bsa_attention_cuda
+
+    B, H, S, D = 1, 8, 4864, 128
+    nb = S // 64
+    q, kk, v = (_rand((B, H, S, D), torch.bfloat16, s, cuda) for s in (100 + k, 110 + k, 120 + k))
+    idx = _random_indices(B, H, nb, k, 130 + k)
+    out = bsa_attention_cuda(q, kk, v, torch.from_numpy(idx).to(cuda), chunk_thw=(1, 1, 64), shape=(1, 1, S))
+    torch.cuda.synchronize()
+    ref = orc.bsa_sparse_attention(_np(q), _np(kk), _np(v), idx, (1, 1, S), (1, 1, 64))
+    _close(_np(out), ref)
+
+
+def test_misaligned_view_runs_the_engine(cuda):
+    """A view the TMA maps cannot read in place (base 2 bytes past a 16-byte boundary) is copied once by
+    the host layer and computed by the engine: bit-identical to the contiguous call, no dense fallback."""
+    from longcat_video.models.block_sparse_attention import bsa_attention
+
+    B, H, S, D = 1, 2, 512, 128
+    flat = _rand((3 * B * H * S * D + 1,), torch.bfloat16, 140, cuda)
+    q, k, v = (flat[1 + i * B * H * S * D:1 + (i + 1) * B * H * S * D].view(B, H, S, D) for i in range(3))
+    a, ia = bsa_attention(q, k, v, (8, 8, 8), chunk_thw=(4, 4, 4), topk=3, return_indices=True)
+    b, ib = bsa_attention(q.clone(), k.clone(), v.clone(), (8, 8, 8), chunk_thw=(4, 4, 4), topk=3,
+                          return_indices=True)
+    assert torch.equal(ia, ib) and torch.equal(a, b)

@@ -255,3 +255,66 @@ def test_batched_dit_views_are_merged_before_the_kernel():
     assert _native._merge_batch(c) is c
     heads_view = torch.randn(B, 2 * H, N, D)[:, :H]  # a head slice keeps stride(0) = 2H * stride(1)
     assert _native._merge_batch(heads_view).stride(0) == H * heads_view.stride(1)
+
+
+# ------------------------------------------------------------------ the hook's dense fallback
+def _hook_attn(monkeypatch, exc):
+    from longcat_video.models import attention as attn_mod
+
+    def fake_bsa(*_a, **_k):
+        raise exc
+
+    monkeypatch.setattr(attn_mod, "bsa_attention", fake_bsa)
+    torch.manual_seed(0)
+    a = attn_mod.Attention(64, 2)
+    a.enable_bsa = True
+    return a
+
+
+def test_hook_falls_back_to_dense_only_on_shape_errors(monkeypatch):
+    from longcat_video._native import BSAShapeError
+
+    a = _hook_attn(monkeypatch, BSAShapeError("Latent shape (4, 4, 6) must be a multiple of chunk_thw (4, 4, 4)"))
+    q, k, v = (torch.randn(1, 2, 96, 32) for _ in range(3))
+    out = a._process_attn(q, k, v, shape=(4, 4, 6))
+    assert torch.allclose(out, torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=a.scale))
+
+
+@pytest.mark.parametrize("exc", [ValueError("head_dim D=136 must be a multiple of 8 in [8, 128]"),
+                                 RuntimeError("bsa_forward failed (code 5)")])
+def test_hook_does_not_swallow_engine_errors(monkeypatch, exc):
+    a = _hook_attn(monkeypatch, exc)
+    q, k, v = (torch.randn(1, 2, 64, 32) for _ in range(3))
+    with pytest.raises(type(exc)):
+        a._process_attn(q, k, v, shape=(4, 4, 4))
+
+
+def test_real_shape_error_reaches_dense_path():
+    """Through the real engine module: the divisibility check runs on the host before any device work,
+    so on a machine without a GPU the hook still lands on dense attention (attention.py:174-179)."""
+    from longcat_video.models.attention import Attention
+
+    torch.manual_seed(0)
+    a = Attention(64, 2)
+    a.enable_bsa = True
+    q, k, v = (torch.randn(1, 2, 96, 32) for _ in range(3))
+    out = a._process_attn(q, k, v, shape=(4, 4, 6))
+    assert torch.allclose(out, torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=a.scale))
+
+
+def test_unreadable_views_are_copied_not_refused():
+    from longcat_video import _native
+
+    base = torch.zeros(2 * 3 * 64 * 128 + 1, dtype=torch.bfloat16)
+    off = base[1:].view(2, 3, 64, 128)  # base address 2 bytes past a 16-byte boundary
+    assert _native._misaligned(off)
+    fixed = _native._merge_batch(off)
+    assert fixed.is_contiguous() and not _native._misaligned(fixed) and torch.equal(fixed, off)
+    assert _native._aligned(off).is_contiguous()
+    ok = torch.zeros(2, 3, 64, 128, dtype=torch.bfloat16)
+    assert _native._merge_batch(ok) is ok and _native._aligned(ok) is ok
+    # DiT view at B > 1: aligned, but batch and head strides do not merge -> copied for attention only
+    qkv = torch.zeros(2, 64, 3, 3, 128, dtype=torch.bfloat16).permute(2, 0, 3, 1, 4)
+    q = qkv[0]
+    assert _native._aligned(q) is q
+    assert _native._merge_batch(q) is not q
