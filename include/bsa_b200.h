@@ -76,6 +76,17 @@ int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t 
 int bsa_score_topk(const float* q_pooled, const float* k_pooled, int BH, int nb, int D, int topk,
                    int32_t* block_indices, float* scores, void* stream);
 
+/* block_routing_scores + topk_block_indices without the score matrix -- block_sparse_attention.py:107-134.
+ * Same indices as bsa_score_topk (the k largest exact fp32 scores, each one fma chain over d; ties to the
+ * smaller block id; ids ascending), computed from tensor-core approximate scores with an error bound and
+ * exact scores for the blocks near each row's threshold.  scratch: bsa_route_scratch_bytes(BH, nb, D)
+ * bytes of caller-owned device memory, 256-byte aligned (bf16 copies of the pooled blocks, their norms
+ * and 16-bit score keys [BH, nb, round_up(nb, 8)]).  nb <= 3072; bsa_route_scratch_bytes returns 0 for
+ * sizes it does not serve. */
+int64_t bsa_route_scratch_bytes(int BH, int nb, int D);
+int bsa_route_topk(const float* q_pooled, const float* k_pooled, int BH, int nb, int D, int topk,
+                   int32_t* block_indices, void* scratch, void* stream);
+
 /* block_routing_scores alone (block_sparse_attention.py:107-112): scores[BH, nq, nk] fp32. */
 int bsa_block_scores(const float* q_pooled, const float* k_pooled, int BH, int nq, int nk, int D, float* scores,
                      void* stream);
@@ -98,9 +109,10 @@ int bsa_attention_indices(const void* q, const void* k, const void* v, const int
 
 /* Full BSA call -- bsa_attention(q, k, v, shape, sparsity, chunk_thw, sm_scale),
  * block_sparse_attention.py:201-250: pool Q and K, score, top-k, sparse attention.
- * scratch: caller-provided device memory of bsa_forward_scratch_bytes() bytes (pooled fp32
- * Q/K, [B*H, nb, D] each, then the fp32 block-score matrix [B*H, nb, nb] with rows padded to a
- * multiple of 4).  block_indices receives the routing ([B,H,nb,topk]).  With rope != NULL, q and k are
+ * scratch: caller-provided device memory of bsa_forward_scratch_bytes() bytes, 256-byte aligned
+ * (pooled fp32 Q/K, [B*H, nb, D] each, then the routing scratch of bsa_route_topk; for nb > 3072 the
+ * fp32 block-score matrix [B*H, nb, nb] with rows padded to a multiple of 4 instead).  block_indices
+ * receives the routing ([B,H,nb,topk]).  With rope != NULL, q and k are
  * pre-RoPE and q_rot / k_rot (contiguous [B,H,S,D]) receive the rotated tensors that the
  * attention then reads. */
 int64_t bsa_forward_scratch_bytes(int B, int H, int S, int D, int cT, int cH, int cW);

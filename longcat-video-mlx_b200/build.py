@@ -18,8 +18,8 @@ REPO = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "longcat_video", "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libbsa_b200.so")
-SOURCES = ["bsa_capi.cu", "bsa_attn.cu", "bsa_score.cu", "bsa_noalloc.cu", "bsa_xfer.cu"]
-HEADERS = ["bsa_ptx.cuh", "bsa_kernels.h"]
+SOURCES = ["bsa_capi.cu", "bsa_attn.cu", "bsa_score.cu", "bsa_route.cu", "bsa_noalloc.cu", "bsa_xfer.cu"]
+HEADERS = ["bsa_ptx.cuh", "bsa_kernels.h", "bsa_select.cuh"]
 
 
 def nvcc_path() -> str:

@@ -118,6 +118,21 @@ int make_map(CUtensorMap* m, const void* base, int dtype, int B, int H, int D, c
   return BSA_OK;
 }
 
+// 3-D map over one bf16 pair array of the routing scratch: (d = 128, block = nb, b*h = BH), box (64, 128, 1).
+int make_pair_map(CUtensorMap* m, const void* base, int nb, int BH) {
+  auto enc = encode_fn();
+  if (!enc) return fail(BSA_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(nb), static_cast<cuuint64_t>(BH)};
+  cuuint64_t strides[2] = {256, static_cast<cuuint64_t>(nb) * 256};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BSA_ERR_ARG, "routing pair map: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return BSA_OK;
+}
+
 // ------------------------------------------------------------------ plans: validated, ready to launch
 struct PoolPlan {
   bsa::PoolArgs a;
@@ -254,7 +269,8 @@ int bsa_device_error(int clear) {
   if (cudaDeviceSynchronize() != cudaSuccess) return cuda_fail("cudaDeviceSynchronize");
   const int a = bsa::attn_device_error(clear);
   const int s = bsa::score_device_error(clear);
-  return a ? a : s;
+  const int r = bsa::route_device_error(clear);
+  return a ? a : (s ? s : r);
 }
 
 int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss, int T,
@@ -283,6 +299,29 @@ int bsa_score_topk(const float* q_pooled, const float* k_pooled, int BH, int nb,
   if (rc == BSA_ERR_CUDA) return cuda_fail("score/top-k kernel launch");
   if (rc) return fail(rc, "score/top-k: unsupported sizes (nb=%d)", nb);
   return BSA_OK;
+}
+
+int64_t bsa_route_scratch_bytes(int BH, int nb, int D) {
+  if (BH <= 0 || !bsa::route_supported(nb, D)) return 0;
+  return bsa::route_scratch_bytes(BH, nb);
+}
+
+int bsa_route_topk(const float* q_pooled, const float* k_pooled, int BH, int nb, int D, int topk,
+                   int32_t* block_indices, void* scratch, void* stream) {
+  if (!q_pooled || !k_pooled || !block_indices || !scratch) return fail(BSA_ERR_ARG, "null pointer");
+  if (BH <= 0 || !bsa::route_supported(nb, D))
+    return fail(BSA_ERR_SHAPE, "bad sizes BH=%d nb=%d D=%d (nb at most 3072; D a multiple of 8, at most 128)", BH,
+                nb, D);
+  if ((reinterpret_cast<uintptr_t>(q_pooled) | reinterpret_cast<uintptr_t>(k_pooled)) & 15u)
+    return fail(BSA_ERR_ALIGN, "pooled blocks must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(scratch) & 255u) return fail(BSA_ERR_ALIGN, "scratch must be 256-byte aligned");
+  if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
+  bsa::RouteArgs a;
+  a.qp = q_pooled; a.kp = k_pooled; a.BH = BH; a.nb = nb; a.D = D; a.topk = topk;
+  a.idx = block_indices; a.scratch = scratch; a.make_pair_map = make_pair_map;
+  const int rc = bsa::launch_route(a, static_cast<cudaStream_t>(stream));
+  if (rc == BSA_ERR_CUDA) return cuda_fail("routing kernel launch");
+  return rc;
 }
 
 int bsa_block_scores(const float* q_pooled, const float* k_pooled, int BH, int nq, int nk, int D, float* scores,
@@ -331,11 +370,16 @@ int bsa_attention_indices_ex(const void* q, const void* k, const void* v, const 
   return attn_run(pl, stream);
 }
 
+// Scratch of bsa_forward: pooled Q and K (fp32, [B*H, nb, D] each, padded to 256 bytes), then the
+// routing scratch (bsa_route_topk) where routing supports the size, else the fp32 score matrix.
 int64_t bsa_forward_scratch_bytes(int B, int H, int S, int D, int cT, int cH, int cW) {
   const int n = cT * cH * cW;
   if (n <= 0 || B <= 0 || H <= 0 || S <= 0 || D <= 0) return 0;
   const int64_t nb = S / n;
-  return 2ll * B * H * nb * D * 4 + static_cast<int64_t>(B) * H * nb * score_ld(static_cast<int>(nb)) * 4;
+  const int64_t pooled = (2ll * B * H * nb * D * 4 + 255) & ~int64_t(255);
+  if (bsa::route_supported(static_cast<int>(nb), D))
+    return pooled + bsa::route_scratch_bytes(B * H, static_cast<int>(nb));
+  return pooled + static_cast<int64_t>(B) * H * nb * score_ld(static_cast<int>(nb)) * 4;
 }
 
 int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
@@ -358,7 +402,7 @@ int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B
   if (sm_reserve < 0) return fail(BSA_ERR_ARG, "sm_reserve=%d must be >= 0", sm_reserve);
   if (!q || !k || !v || !scratch || !block_indices || !out || !q_strides || !k_strides || !v_strides || !out_strides)
     return fail(BSA_ERR_ARG, "null pointer");
-  if (!aligned16(scratch)) return fail(BSA_ERR_ALIGN, "scratch must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(scratch) & 255u) return fail(BSA_ERR_ALIGN, "scratch must be 256-byte aligned");
   if (dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
     return fail(BSA_ERR_DTYPE, "sparse attention supports fp16 and bf16 inputs (dtype code %d)", dtype);
   if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(BSA_ERR_SHAPE, "empty tensor");
@@ -378,10 +422,15 @@ int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B
   if ((rc = pool_plan(pk, k, dtype, B, H, S, D, k_strides[0], k_strides[1], k_strides[2], T, Hl, Wl, cT, cH, cW, rope,
                       rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, k_rot, kp)))
     return rc;
+  void* rest = static_cast<uint8_t*>(scratch) + ((2ll * B * H * nb * D * 4 + 255) & ~int64_t(255));
+  const bool route = bsa::route_supported(nb, D);
+  bsa::RouteArgs ra;
+  ra.qp = qp; ra.kp = kp; ra.BH = B * H; ra.nb = nb; ra.D = D; ra.topk = topk;
+  ra.idx = block_indices; ra.scratch = rest; ra.make_pair_map = make_pair_map;
   bsa::ScoreArgs sa;
   sa.qp = qp; sa.kp = kp; sa.BH = B * H; sa.nq = nb; sa.nk = nb; sa.D = D; sa.topk = topk;
   sa.idx = block_indices; sa.ldc = static_cast<int>(score_ld(nb));
-  sa.scores = kp + static_cast<int64_t>(B) * H * nb * D;
+  sa.scores = static_cast<float*>(rest);
   AttnPlan pa;
   if (rope) {
     // the attention reads the rotated tensors the pool kernels write (contiguous [B,H,S,D])
@@ -396,9 +445,10 @@ int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B
   // ---- launches
   if ((rc = pool_run(pq, stream))) return rc;
   if ((rc = pool_run(pk, stream))) return rc;
-  rc = bsa::launch_score_topk(sa, static_cast<cudaStream_t>(stream));
-  if (rc == BSA_ERR_CUDA) return cuda_fail("score/top-k kernel launch");
-  if (rc) return fail(rc, "score/top-k: unsupported sizes (nb=%d)", nb);
+  rc = route ? bsa::launch_route(ra, static_cast<cudaStream_t>(stream))
+             : bsa::launch_score_topk(sa, static_cast<cudaStream_t>(stream));
+  if (rc == BSA_ERR_CUDA) return cuda_fail("routing kernel launch");
+  if (rc) return rc == BSA_ERR_ARG ? rc : fail(rc, "routing: unsupported sizes (nb=%d)", nb);
   return attn_run(pa, stream);
 }
 

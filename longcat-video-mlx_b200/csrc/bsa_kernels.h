@@ -38,6 +38,23 @@ int launch_score_topk(const ScoreArgs& a, cudaStream_t stream);
 int launch_scores_only(const ScoreArgs& a, cudaStream_t stream);
 int launch_topk(const float* scores, int rows, int nk, int ldc, int topk, int32_t* idx, cudaStream_t stream);
 
+// ------------------------------------------------------------------ routing without the score matrix
+// (bsa_route.cu): the same indices as launch_score_topk, from tensor-core approximate scores and exact
+// fp32 scores for the blocks near each row's threshold.
+struct RouteArgs {
+  const float* qp;       // [BH, nb, D] fp32
+  const float* kp;       // [BH, nb, D] fp32
+  int BH, nb, D, topk;
+  int32_t* idx;          // [BH, nb, topk], ascending block ids
+  void* scratch;         // route_scratch_bytes(BH, nb), 256-byte aligned
+  // builds a 3-D bf16 map (d = 128, block = nb, b*h = BH) with 64 x 128 boxes over one pair array
+  int (*make_pair_map)(CUtensorMap* m, const void* base, int nb, int BH);
+};
+bool route_supported(int nb, int D);
+int64_t route_scratch_bytes(int BH, int nb);
+int launch_route(const RouteArgs& a, cudaStream_t stream);
+int route_device_error(int clear);
+
 // ------------------------------------------------------------------ sparse attention
 struct AttnArgs {
   const int32_t* idx;

@@ -184,6 +184,17 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (both operands from shared-memory descriptors).
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // 16 lanes x 32 bit, two column runs: threads 0-15 read lanes (taddr.lane + t) at columns
 // [taddr.col, +64), threads 16-31 the same lanes at columns [taddr.col + 64, +64).
 __device__ __forceinline__ void tmem_ld_16x2_x64(uint32_t taddr, uint32_t* r) {

@@ -1,0 +1,524 @@
+// Block routing (block_routing_scores + topk_block_indices, block_sparse_attention.py:107-134) without
+// the block-score matrix.  The selected indices are exactly those of the exact fp32 scores (one fma
+// chain over d = 0..D-1 per score, as in bsa_score.cu and the CPU oracle) followed by top-k with ties
+// to the smaller block id; the score matrix itself is never written.
+//
+//   1. split  : pooled fp32 Q/K rows -> bf16 pairs (hi = bf16(x), lo = bf16(x - hi)), zero padded to
+//               128 columns, and an upper bound of each row's l2 norm (+inf for values this bound does
+//               not cover: non-finite, above 2^60 or below 2^-60 in magnitude).
+//   2. keys   : tcgen05 approximate scores a = qh.kh + qh.kl + ql.kh (fp32 accumulation in TMEM), 128
+//               query blocks x 128 key blocks per step, written as 16-bit keys: the top half of the
+//               score's order-preserving 32-bit pattern (so a key names an interval of fp32 scores).
+//   3. select : one warp per row.  With T = the k-th largest key of the row, the exact k-th largest
+//               score s_(k) lies in [L, U] = [low(T) - e, high(T) + e] (e bounds |a - s|, below).  A
+//               block whose interval lies above U is selected, one below L is not; only the blocks
+//               whose interval meets the band get the exact score, and the top of those fills the
+//               remaining places (ties to the smaller id).  Rows whose band holds more than kMaxBand
+//               blocks, or whose bound is not finite, are scored exactly in full (same result).
+//
+// Error bound.  With x = hi + lo + r, |r| <= 2^-18 |x| (two round-to-nearest bf16 steps), the three
+// products drop lo*lo and the r terms: at most ~3.1 * 2^-18 sum_d |q_d k_d|.  bf16 products are exact
+// in fp32; the tensor core's fp32 accumulation of 3 x 128 terms adds at most ~2^-14.3 sum_d |q_d k_d|
+// even with truncation at every addition, and the exact fma chain itself is within 128 * 2^-24 of the
+// real dot product.  So |a - s| <= 2^-13.9 sum_d |q_d k_d| <= 2^-13.9 |q| |k|, and e = 2^-12 |q| max|k|
+// (with |q|, |k| rounded up) leaves a margin of about 3.7x.
+#include <cstdint>
+#include <mutex>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include "bsa_kernels.h"
+#include "bsa_ptx.cuh"
+#include "bsa_select.cuh"
+
+namespace bsa {
+
+__device__ int g_route_err;
+
+namespace route {
+constexpr int kDP = 128;                 // padded head dim of the bf16 pairs
+constexpr float kErrC = 1.0f / 4096.0f;  // e = kErrC * |q| * max|k|
+constexpr int kMaxBand = 64;             // blocks per row scored exactly on the fast path
+
+// ------------------------------------------------------------------ 1. split
+// One warp per pooled row (Q rows then K rows); lane l holds d = 4l .. 4l+3.
+__global__ void __launch_bounds__(256) split_kernel(const float* __restrict__ qp, const float* __restrict__ kp,
+                                                    int rows, int nb, int D, __nv_bfloat16* hl, float* nrm,
+                                                    float* nkmax) {
+  const int lane = threadIdx.x & 31;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < 2 * rows; r += nw) {
+    const int which = r >= rows;  // 0: Q, 1: K
+    const int row = r - which * rows;
+    const float* src = (which ? kp : qp) + static_cast<long long>(row) * D;
+    const int d0 = 4 * lane;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    if (d0 < D) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src + d0));
+      x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+    }
+    __nv_bfloat16 hi[4], lo[4];
+    float n2 = 0.f;
+    bool extreme = false;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      hi[e] = __float2bfloat16_rn(x[e]);
+      lo[e] = __float2bfloat16_rn(__fsub_rn(x[e], __bfloat162float(hi[e])));
+      n2 = fmaf(x[e], x[e], n2);
+      const float a = fabsf(x[e]);
+      extreme |= !(a <= 1.152921504606847e18f) || (a != 0.f && a < 8.673617379884035e-19f);  // 2^60, 2^-60
+    }
+    __nv_bfloat16* dh = hl + (static_cast<long long>(2 * which) * rows + row) * kDP + d0;
+    __nv_bfloat16* dl = hl + (static_cast<long long>(2 * which + 1) * rows + row) * kDP + d0;
+    *reinterpret_cast<uint2*>(dh) = *reinterpret_cast<const uint2*>(hi);
+    *reinterpret_cast<uint2*>(dl) = *reinterpret_cast<const uint2*>(lo);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, off);
+    extreme = __any_sync(0xffffffffu, extreme);
+    if (lane == 0) {
+      // sqrt of an fp32 sum of 128 squares: relative error far below 2^-10, so the bound holds
+      const float n = extreme ? INFINITY : __fmul_ru(sqrtf(n2), 1.0009765625f);
+      nrm[static_cast<long long>(which) * rows + row] = n;
+      if (which) atomicMax(reinterpret_cast<int*>(nkmax) + row / nb, __float_as_int(n));  // n >= 0
+    }
+  }
+}
+
+// ------------------------------------------------------------------ 2. keys (tcgen05)
+constexpr int kTile = 128;                          // query blocks per CTA, key blocks per step
+constexpr int kArrBytes = kTile * kDP * 2;          // 32 KB: one bf16 array tile (two 16 KB d-halves)
+constexpr int kKeyThreads = 320;                    // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+struct KeySmem {
+  uint64_t a_full;
+  uint64_t b_full[2], b_empty[2];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr int kKeyTiles = 2 * kArrBytes + 2 * 2 * kArrBytes;  // A (qh, ql) + two B stages (kh, kl)
+constexpr int kKeySmemBytes = 1024 + kKeyTiles + static_cast<int>(sizeof(KeySmem));
+
+__device__ __forceinline__ uint32_t key16(float a) {
+  if (a != a) return 1u;  // NaN: the lowest real key (its interval bounds are NaN: never outside a band)
+  return topk::ordered_key(a) >> 16;
+}
+
+__global__ void __launch_bounds__(kKeyThreads, 1)
+    key_kernel(const __grid_constant__ CUtensorMap m_qh, const __grid_constant__ CUtensorMap m_ql,
+               const __grid_constant__ CUtensorMap m_kh, const __grid_constant__ CUtensorMap m_kl, int nb, int ldk,
+               uint16_t* keys) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* sA = sm;                       // qh | ql
+  uint8_t* sB = sm + 2 * kArrBytes;       // stage s: kh | kl at sB + s * 2 * kArrBytes
+  KeySmem& ks = *reinterpret_cast<KeySmem*>(sm + kKeyTiles);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int i0 = blockIdx.x * kTile;
+  const int nch = (nb + kTile - 1) / kTile;
+  if (threadIdx.x == 0) {
+    mbar_init(&ks.a_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&ks.b_full[s], 1);
+      mbar_init(&ks.b_empty[s], 1);
+      mbar_init(&ks.acc_full[s], 1);
+      mbar_init(&ks.acc_empty[s], 8);
+    }
+    mbar_init(&ks.drain, 1);
+    ks.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&ks.tmem_base, 256);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ks.tmem_base;
+  volatile int* abort_flag = &ks.abort_flag;
+  int* err = &g_route_err;
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&ks.a_full, 2 * kArrBytes);
+      for (int hh = 0; hh < 2; ++hh) {
+        tma_load_3d(sA + hh * 16384, &m_qh, &ks.a_full, 64 * hh, i0, bh);
+        tma_load_3d(sA + kArrBytes + hh * 16384, &m_ql, &ks.a_full, 64 * hh, i0, bh);
+      }
+      int c = 0;
+      for (; c < nch; ++c) {
+        const int s = c & 1;
+        if (c >= 2 && !mbar_wait(&ks.b_empty[s], static_cast<uint32_t>(((c >> 1) - 1) & 1), abort_flag, err, 401))
+          break;
+        uint8_t* dst = sB + s * 2 * kArrBytes;
+        mbar_arrive_expect_tx(&ks.b_full[s], 2 * kArrBytes);
+        for (int hh = 0; hh < 2; ++hh) {
+          tma_load_3d(dst + hh * 16384, &m_kh, &ks.b_full[s], 64 * hh, c * kTile, bh);
+          tma_load_3d(dst + kArrBytes + hh * 16384, &m_kl, &ks.b_full[s], 64 * hh, c * kTile, bh);
+        }
+      }
+      // teardown: every TMA write into shared memory has landed
+      const uint64_t t0 = globaltimer_ns();
+      for (int cc = (c > 2 ? c - 2 : 0); cc < c; ++cc)
+        while (!mbar_try_wait(&ks.b_full[cc & 1], static_cast<uint32_t>((cc >> 1) & 1)) &&
+               globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
+      while (!mbar_try_wait(&ks.a_full, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(128, 128, 1, 0, 0);
+      bool ok = mbar_wait(&ks.a_full, 0, abort_flag, err, 402);
+      for (int c = 0; c < nch && ok; ++c) {
+        const int s = c & 1;
+        ok = mbar_wait(&ks.b_full[s], static_cast<uint32_t>((c >> 1) & 1), abort_flag, err, 403);
+        if (ok && c >= 2)
+          ok = mbar_wait(&ks.acc_empty[s], static_cast<uint32_t>(((c >> 1) - 1) & 1), abort_flag, err, 404);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(s * kTile);
+        const uint32_t aq = smem_u32(sA), bq = smem_u32(sB + s * 2 * kArrBytes);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          const uint64_t a_hi = sdesc_sw128(aq + off, 16, 1024), a_lo = sdesc_sw128(aq + kArrBytes + off, 16, 1024);
+          const uint64_t b_hi = sdesc_sw128(bq + off, 16, 1024), b_lo = sdesc_sw128(bq + kArrBytes + off, 16, 1024);
+          umma_ss(d, a_hi, b_hi, idesc, kk > 0 ? 1u : 0u);
+          umma_ss(d, a_hi, b_lo, idesc, 1u);
+          umma_ss(d, a_lo, b_hi, idesc, 1u);
+        }
+        umma_commit(&ks.acc_full[s]);
+        umma_commit(&ks.b_empty[s]);
+      }
+      umma_commit(&ks.drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&ks.drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // epilogue: warp w reads TMEM lane quarter w % 4 (query blocks 32q .. 32q+31 of the tile) and
+    // columns [64ch, 64ch + 64) of each 128-column step
+    const int q = warp & 3;
+    const int ch = (warp - 2) >> 2;
+    const int i = i0 + 32 * q + lane;
+    uint16_t* krow = keys + (static_cast<long long>(bh) * nb + (i < nb ? i : 0)) * ldk;
+    for (int c = 0; c < nch; ++c) {
+      const int s = c & 1;
+      bool ok = mbar_wait(&ks.acc_full[s], static_cast<uint32_t>((c >> 1) & 1), abort_flag, err, 405);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int part = 0; part < 2; ++part) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(s * kTile + 64 * ch + 32 * part),
+                  r);
+        tmem_ld_wait();
+        const int j0 = c * kTile + 64 * ch + 32 * part;
+        if (i < nb) {
+#pragma unroll
+          for (int e8 = 0; e8 < 4; ++e8) {
+            if (j0 + 8 * e8 < ldk) {  // ldk is a multiple of 8; keys past nb in the row are never read
+              uint4 w;
+              w.x = key16(__uint_as_float(r[8 * e8 + 0])) | (key16(__uint_as_float(r[8 * e8 + 1])) << 16);
+              w.y = key16(__uint_as_float(r[8 * e8 + 2])) | (key16(__uint_as_float(r[8 * e8 + 3])) << 16);
+              w.z = key16(__uint_as_float(r[8 * e8 + 4])) | (key16(__uint_as_float(r[8 * e8 + 5])) << 16);
+              w.w = key16(__uint_as_float(r[8 * e8 + 6])) | (key16(__uint_as_float(r[8 * e8 + 7])) << 16);
+              *reinterpret_cast<uint4*>(krow + j0 + 8 * e8) = w;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ks.acc_empty[s]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------------ 3. select (one warp per row)
+constexpr int kSelThreads = 256;
+struct SelWarp {
+  uint32_t hist[256];
+  uint32_t cand[topk::kCand];
+  float q[kDP];
+  int32_t band_id[kMaxBand];
+  uint8_t band_sel[kMaxBand];
+};
+
+// fp32 value of an order-preserving bit pattern
+__device__ __forceinline__ float from_ordered(uint32_t o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+
+// exact score: one fp32 fma chain over d = 0..D-1, starting at 0 (block_routing_scores, in the order
+// the CPU oracle uses)
+__device__ __forceinline__ float exact_score(const float* q, const float* __restrict__ krow, int D) {
+  float acc = 0.f;
+  for (int d = 0; d < D; d += 4) {
+    const float4 kv = __ldg(reinterpret_cast<const float4*>(krow + d));
+    acc = fmaf(q[d], kv.x, acc);
+    acc = fmaf(q[d + 1], kv.y, acc);
+    acc = fmaf(q[d + 2], kv.z, acc);
+    acc = fmaf(q[d + 3], kv.w, acc);
+  }
+  return acc;
+}
+
+// The same chain for two rows at once (row1 may be null), 16 d values per round: every load of a
+// round is issued before its first fma, so a round costs one L2 latency instead of four.
+__device__ __forceinline__ void exact_score2(const float* q, const float* __restrict__ r0, const float* __restrict__ r1,
+                                             int D, float& s0, float& s1) {
+  float a0 = 0.f, a1 = 0.f;
+  for (int d0 = 0; d0 < D; d0 += 16) {
+    float4 k0[4], k1[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int d = d0 + 4 * c;
+      k0[c] = d < D ? __ldg(reinterpret_cast<const float4*>(r0 + d)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      k1[c] = (r1 && d < D) ? __ldg(reinterpret_cast<const float4*>(r1 + d)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int d = d0 + 4 * c;
+      if (d < D) {
+        a0 = fmaf(q[d], k0[c].x, a0); a0 = fmaf(q[d + 1], k0[c].y, a0);
+        a0 = fmaf(q[d + 2], k0[c].z, a0); a0 = fmaf(q[d + 3], k0[c].w, a0);
+        a1 = fmaf(q[d], k1[c].x, a1); a1 = fmaf(q[d + 1], k1[c].y, a1);
+        a1 = fmaf(q[d + 2], k1[c].z, a1); a1 = fmaf(q[d + 3], k1[c].w, a1);
+      }
+    }
+  }
+  s0 = a0;
+  s1 = a1;
+}
+
+// Key thresholds of a band [L, U] with error bound e: keys >= *ks are above U (sure), finite keys
+// <= *ko are below L (out).  Both bounds are monotone in the key over the finite keys [0x80, 0xff80],
+// so each is a 16-step binary search.  Keys below 0x80 (NaN, -inf) are never sure nor out.
+__device__ __forceinline__ void band_keys(float L, float U, float e, uint32_t& ks, uint32_t& ko) {
+  uint32_t lo = 0x80u, hi = 0xff81u;  // smallest sure key in [lo, hi]; 0xff81: none
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (__fsub_rd(from_ordered(mid << 16), e) > U) hi = mid;
+    else lo = mid + 1u;
+  }
+  ks = lo;
+  lo = 0x7fu;  // largest out key in [lo, hi]; 0x7f: none
+  hi = 0xff80u;
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi + 1u) >> 1;
+    if (__fadd_ru(from_ordered((mid << 16) | 0xffffu), e) < L) lo = mid;
+    else hi = mid - 1u;
+  }
+  ko = lo;
+}
+
+template <int PL>
+__global__ void __launch_bounds__(kSelThreads, 2)
+    select_kernel(const uint16_t* __restrict__ keys, int ldk, const float* __restrict__ qp,
+                  const float* __restrict__ kp, const float* __restrict__ nrm, const float* __restrict__ nkmax, int rows,
+                  int nb, int D, int k, int32_t* idx) {
+  __shared__ SelWarp sw_all[kSelThreads / 32];
+  const int lane = threadIdx.x & 31;
+  SelWarp& sw = sw_all[threadIdx.x >> 5];
+  const uint32_t lt = (1u << lane) - 1u;
+  const int nw = gridDim.x * (kSelThreads / 32);
+  for (int row = blockIdx.x * (kSelThreads / 32) + (threadIdx.x >> 5); row < rows; row += nw) {
+    const int bh = row / nb;
+    int32_t* out = idx + static_cast<long long>(row) * k;
+    if (k == nb) {  // every block: the ids in order
+      for (int j = lane; j < nb; j += 32) out[j] = j;
+      continue;
+    }
+    const float* kbase = kp + static_cast<long long>(bh) * nb * D;
+    // this row's q block, for the exact scores
+    __syncwarp();
+    for (int d = lane; d < D; d += 32) sw.q[d] = __ldg(qp + static_cast<long long>(row) * D + d);
+    const uint16_t* krow = keys + static_cast<long long>(row) * ldk;
+    uint32_t key[PL];
+#pragma unroll
+    for (int e = 0; e < PL; ++e) {
+      const int j = lane + 32 * e;
+      key[e] = j < nb ? static_cast<uint32_t>(__ldg(krow + j)) : 0u;
+    }
+    const float ebound = __fmul_ru(__fmul_ru(kErrC, __ldg(nrm + row)), __ldg(nkmax + bh));
+    int need;
+    uint32_t eqc;
+    const uint32_t T = topk::kth_largest<PL>(key, nb, k, lane, sw.hist, sw.cand, need, eqc);
+    // s_(k) in [L, U]; a key's interval is [from_ordered(key << 16), from_ordered(key << 16 | 0xffff)]
+    const float L = __fsub_rd(from_ordered(T << 16), ebound);
+    const float U = __fadd_ru(from_ordered((T << 16) | 0xffffu), ebound);
+    uint32_t ks, ko;
+    band_keys(L, U, ebound, ks, ko);
+    // key classes: sure (key >= ks), out (0x80 <= key <= ko), band (the rest of the valid keys)
+    auto is_sure = [&](uint32_t u) { return u >= ks; };
+    auto is_band = [&](uint32_t u) { return u != 0u && u < ks && (u > ko || u < 0x80u); };
+    int n_sure = 0, n_band = 0;
+#pragma unroll
+    for (int e = 0; e < PL; ++e) {
+      n_sure += __popc(__ballot_sync(0xffffffffu, is_sure(key[e])));
+      n_band += __popc(__ballot_sync(0xffffffffu, is_band(key[e])));
+    }
+    const bool fast = ebound < INFINITY && n_band <= kMaxBand && n_sure <= k && n_sure + n_band >= k;
+    int taken = 0;
+    __syncwarp();
+    if (fast) {
+      // the band's block ids, ascending
+      int pos = 0;
+#pragma unroll
+      for (int e = 0; e < PL; ++e) {
+        const bool band = is_band(key[e]);
+        const uint32_t bb = __ballot_sync(0xffffffffu, band);
+        if (band) sw.band_id[pos + __popc(bb & lt)] = lane + 32 * e;
+        pos += __popc(bb);
+      }
+      __syncwarp();
+      // exact scores of the band (two per lane at most), as order-preserving keys
+      uint32_t ek[2] = {0u, 0u};
+      if (lane < n_band) {
+        float s0, s1;
+        const float* r1 = lane + 32 < n_band ? kbase + static_cast<long long>(sw.band_id[lane + 32]) * D : nullptr;
+        exact_score2(sw.q, kbase + static_cast<long long>(sw.band_id[lane]) * D, r1, D, s0, s1);
+        ek[0] = topk::ordered_key(s0);
+        if (r1) ek[1] = topk::ordered_key(s1);
+      }
+      // the `rest` largest of the band (ties to the smaller id): binary search for the threshold key
+      const int rest = k - n_sure;
+      auto count_ge = [&](uint32_t t) -> int {
+        return __reduce_add_sync(0xffffffffu, (ek[0] >= t ? 1 : 0) + (ek[1] >= t ? 1 : 0));
+      };
+      uint32_t T2 = 0xffffffffu;
+      int take_eq = 0;
+      if (rest > 0) {
+        uint32_t lo = 1u, hi = 0xffffffffu;
+        while (lo < hi) {
+          const uint32_t mid = lo + ((hi - lo) >> 1) + 1u;
+          if (count_ge(mid) >= rest) lo = mid;
+          else hi = mid - 1u;
+        }
+        T2 = lo;
+        take_eq = rest - (T2 != 0xffffffffu ? count_ge(T2 + 1u) : 0);
+      }
+      const bool eq0 = rest > 0 && ek[0] == T2, eq1 = rest > 0 && ek[1] == T2;
+      const uint32_t b0 = __ballot_sync(0xffffffffu, eq0), b1 = __ballot_sync(0xffffffffu, eq1);
+      const int r0 = __popc(b0 & lt), r1 = __popc(b0) + __popc(b1 & lt);
+      if (lane < n_band) sw.band_sel[lane] = rest > 0 && (ek[0] > T2 || (eq0 && r0 < take_eq));
+      if (lane + 32 < n_band) sw.band_sel[lane + 32] = rest > 0 && (ek[1] > T2 || (eq1 && r1 < take_eq));
+      __syncwarp();
+      // ascending emission: sure blocks and the chosen band blocks
+      int bpos = 0;
+#pragma unroll
+      for (int e = 0; e < PL; ++e) {
+        if (32 * e >= nb) break;  // warp-uniform
+        const uint32_t u = key[e];
+        const bool band = is_band(u);
+        const uint32_t bb = __ballot_sync(0xffffffffu, band);
+        const bool sel = is_sure(u) || (band && sw.band_sel[bpos + __popc(bb & lt)]);
+        const uint32_t sb = __ballot_sync(0xffffffffu, sel);
+        if (sel) out[taken + __popc(sb & lt)] = lane + 32 * e;
+        taken += __popc(sb);
+        bpos += __popc(bb);
+      }
+    } else {
+      // the whole row scored exactly, then the same selection as the top-k kernel
+#pragma unroll
+      for (int e = 0; e < PL; ++e) {
+        const int j = lane + 32 * e;
+        key[e] = j < nb ? topk::ordered_key(exact_score(sw.q, kbase + static_cast<long long>(j) * D, D)) : 0u;
+      }
+      taken = topk::select_emit<PL>(key, nb, k, lane, sw.hist, sw.cand, out);
+    }
+    if (lane == 0 && taken != k) atomicCAS(&g_route_err, 0, 410);
+  }
+}
+
+}  // namespace route
+
+int64_t route_scratch_bytes(int BH, int nb) {
+  const int64_t rows = static_cast<int64_t>(BH) * nb;
+  const int64_t ldk = (static_cast<int64_t>(nb) + 7) & ~int64_t(7);
+  auto up = [](int64_t b) { return (b + 255) & ~int64_t(255); };
+  return up(4 * rows * route::kDP * 2) + up(2 * rows * 4) + up(static_cast<int64_t>(BH) * 4) + up(rows * ldk * 2);
+}
+
+bool route_supported(int nb, int D) { return nb >= 1 && nb <= 3072 && D >= 8 && D <= 128 && D % 8 == 0; }
+
+int launch_route(const RouteArgs& a, cudaStream_t stream) {
+  using namespace route;
+  if (!route_supported(a.nb, a.D) || !a.scratch) return BSA_ERR_SHAPE;
+  const int rows = a.BH * a.nb;
+  const int64_t ldk = (static_cast<int64_t>(a.nb) + 7) & ~int64_t(7);
+  auto up = [](int64_t b) { return (b + 255) & ~int64_t(255); };
+  uint8_t* base = static_cast<uint8_t*>(a.scratch);
+  __nv_bfloat16* hl = reinterpret_cast<__nv_bfloat16*>(base);
+  base += up(4ll * rows * kDP * 2);
+  float* nrm = reinterpret_cast<float*>(base);
+  base += up(2ll * rows * 4);
+  float* nkmax = reinterpret_cast<float*>(base);
+  base += up(static_cast<int64_t>(a.BH) * 4);
+  uint16_t* keys = reinterpret_cast<uint16_t*>(base);
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BSA_ERR_CUDA;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // 1. split (+ the per-head maximum key norm, which starts at 0)
+  if (cudaMemsetAsync(nkmax, 0, static_cast<size_t>(a.BH) * 4, stream) != cudaSuccess) return BSA_ERR_CUDA;
+  {
+    long long grid = (2ll * rows + 7) / 8;
+    if (grid > static_cast<long long>(sms) * 16) grid = static_cast<long long>(sms) * 16;
+    split_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(a.qp, a.kp, rows, a.nb, a.D, hl, nrm, nkmax);
+  }
+  // 2. keys: four 3-D maps (d, block, b*h) over the bf16 arrays, 64 x 128 boxes
+  {
+    CUtensorMap maps[4];
+    for (int m = 0; m < 4; ++m) {
+      const int rc = a.make_pair_map(&maps[m], hl + static_cast<long long>(m) * rows * kDP, a.nb, a.BH);
+      if (rc) return rc;
+    }
+    static std::mutex mu;
+    static bool configured[64] = {};
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (dev >= 64 || !configured[dev]) {
+        if (cudaFuncSetAttribute(key_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kKeySmemBytes) != cudaSuccess)
+          return BSA_ERR_CUDA;
+        if (dev < 64) configured[dev] = true;
+      }
+    }
+    const dim3 grid((a.nb + kTile - 1) / kTile, a.BH, 1);
+    if (grid.y > 65535u) return BSA_ERR_SHAPE;
+    key_kernel<<<grid, kKeyThreads, kKeySmemBytes, stream>>>(maps[0], maps[1], maps[2], maps[3], a.nb,
+                                                             static_cast<int>(ldk), keys);
+  }
+  // 3. select
+  {
+    long long grid = (static_cast<long long>(rows) + 7) / 8;
+    if (grid > static_cast<long long>(sms) * 8) grid = static_cast<long long>(sms) * 8;
+    if (a.nb <= 32 * 48)
+      select_kernel<48><<<static_cast<unsigned>(grid), kSelThreads, 0, stream>>>(
+          keys, static_cast<int>(ldk), a.qp, a.kp, nrm, nkmax, rows, a.nb, a.D, a.topk, a.idx);
+    else
+      select_kernel<96><<<static_cast<unsigned>(grid), kSelThreads, 0, stream>>>(
+          keys, static_cast<int>(ldk), a.qp, a.kp, nrm, nkmax, rows, a.nb, a.D, a.topk, a.idx);
+  }
+  return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
+}
+
+int route_device_error(int clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_route_err, sizeof(int)) != cudaSuccess) return BSA_ERR_CUDA;
+  if (clear && v) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_route_err, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace bsa

@@ -23,6 +23,7 @@
 #include <cuda_fp16.h>
 #include "bsa_kernels.h"
 #include "bsa_ptx.cuh"
+#include "bsa_select.cuh"
 
 namespace bsa {
 
@@ -583,81 +584,14 @@ __global__ void __launch_bounds__(kThreads, 2) score_gemm_kernel(Args a) {
 namespace topk {
 constexpr int kThreads = 256;
 
-__device__ __forceinline__ uint32_t ordered_key(float s) {
-  // -0.0 and +0.0 are one score; NaN sorts below every number (key 1); key 0 marks padding
-  if (s != s) return 1u;
-  const uint32_t u = __float_as_uint(s == 0.0f ? 0.0f : s);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
 struct Args {
   const float* scores;  // rows of length nk, stride ldc
   int rows, nk, ldc, topk;
   int32_t* idx;         // [rows, topk]
 };
 
-constexpr int kCand = 64;  // threshold candidates kept after the first radix digit
-
-// One radix digit (up to 8 bits below `shift`) over NK keys per lane: histogram of the keys that
-// match `prefix` above `shift`, then the digit whose bin holds the need-th largest key.  Updates
-// shift, prefix and need (keys still to take at or below the new prefix); `bincnt` receives the
-// count of the chosen bin (after the last digit: the number of keys equal to the threshold).
-template <int NK>
-__device__ __forceinline__ void radix_pass(const uint32_t (&key)[NK], uint32_t* h, int lane, int& shift,
-                                           uint32_t& prefix, int& need, uint32_t& bincnt) {
-  const int w = shift < 8 ? shift : 8;
-  const int hi_bits = shift;  // keys must match `prefix` above bit `shift`
-  shift -= w;
-  const uint32_t dmask = (1u << w) - 1u;
-  reinterpret_cast<uint4*>(h)[lane * 2] = make_uint4(0u, 0u, 0u, 0u);
-  reinterpret_cast<uint4*>(h)[lane * 2 + 1] = make_uint4(0u, 0u, 0u, 0u);
-  __syncwarp();
-#pragma unroll
-  for (int e = 0; e < NK; ++e) {
-    const uint32_t u = key[e];
-    const bool match = u != 0u && (hi_bits >= 32 || (u >> hi_bits) == (prefix >> hi_bits));
-    if (match) atomicAdd(&h[(u >> shift) & dmask], 1u);
-  }
-  __syncwarp();
-  const uint4 c0 = reinterpret_cast<const uint4*>(h)[lane * 2];
-  const uint4 c1 = reinterpret_cast<const uint4*>(h)[lane * 2 + 1];
-  const uint32_t cnt[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-  uint32_t tot = 0;
-#pragma unroll
-  for (int b = 0; b < 8; ++b) tot += cnt[b];
-  uint32_t suf = tot;  // inclusive suffix sum over lanes >= this lane
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const uint32_t o = __shfl_down_sync(0xffffffffu, suf, off);
-    if (lane + off < 32) suf += o;
-  }
-  const uint32_t above = suf - tot;
-  const bool mine = above < static_cast<uint32_t>(need) && static_cast<uint32_t>(need) <= suf;
-  int digit = 0;
-  uint32_t gt = 0, bc = 0;
-  if (mine) {
-    uint32_t run = above;
-#pragma unroll
-    for (int b = 7; b >= 0; --b) {
-      if (run + cnt[b] >= static_cast<uint32_t>(need)) {
-        digit = lane * 8 + b;
-        gt = run;
-        bc = cnt[b];
-        break;
-      }
-      run += cnt[b];
-    }
-  }
-  const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
-  digit = __shfl_sync(0xffffffffu, digit, src);
-  gt = __shfl_sync(0xffffffffu, gt, src);
-  bincnt = __shfl_sync(0xffffffffu, bc, src);
-  prefix |= static_cast<uint32_t>(digit) << shift;
-  need -= static_cast<int>(gt);
-  __syncwarp();
-}
-
-// PL > 0: the row lives in registers (PL keys per lane, nk <= 32*PL); PL == 0: re-read from memory
+// PL > 0: the row lives in registers (PL keys per lane, nk <= 32*PL) and goes through select_emit
+// (bsa_select.cuh); PL == 0: rows too long for registers are re-read from memory.
 template <int PL>
 __global__ void __launch_bounds__(kThreads, 4) topk_kernel(Args a) {
   const int lane = threadIdx.x & 31;
@@ -665,123 +599,47 @@ __global__ void __launch_bounds__(kThreads, 4) topk_kernel(Args a) {
   if (row >= a.rows) return;
   const float* src = a.scores + static_cast<long long>(row) * a.ldc;
   const int nk = a.nk, k = a.topk;
-  uint32_t key[PL > 0 ? PL : 1];
-  if (PL > 0) {
+  int32_t* out = a.idx + static_cast<long long>(row) * k;
+  int taken = 0;
+  if constexpr (PL > 0) {
+    __shared__ __align__(16) uint32_t hist_all[kThreads / 32][256];
+    __shared__ uint32_t cand_all[kThreads / 32][kCand];
+    uint32_t key[PL];
 #pragma unroll
     for (int e = 0; e < PL; ++e) {
       const int j = lane + 32 * e;
       key[e] = j < nk ? ordered_key(__ldg(src + j)) : 0u;
     }
-  }
-  // number of keys >= t (t >= 1, so padding keys of 0 never count)
-  auto count_ge = [&](uint32_t t) -> int {
-    int c = 0;
-    if (PL > 0) {
-#pragma unroll
-      for (int e = 0; e < (PL > 0 ? PL : 1); ++e) c += key[e] >= t ? 1 : 0;
-    } else {
-      for (int j = lane; j < nk; j += 32) c += ordered_key(__ldg(src + j)) >= t ? 1 : 0;
-    }
-    return __reduce_add_sync(0xffffffffu, c);
-  };
-  uint32_t T;
-  int need;
-  uint32_t eqc = 0;  // number of keys equal to T (radix path)
-  if constexpr (PL > 0) {
-    // Radix select: 8-bit digits, starting below the bits that every key of the row shares
-    // (from the row's min and max key), counted in a per-warp shared histogram.  After the first
-    // digit only the keys of the chosen bin can still be the threshold; for rows of up to 48 keys
-    // per lane with at most kCand such keys, they are compacted (in index order) and the later
-    // digits run on those alone (385 -> 352 us at config 2).
-    __shared__ __align__(16) uint32_t hist_all[kThreads / 32][256];
-    __shared__ uint32_t cand_all[kThreads / 32][kCand];
-    uint32_t* h = hist_all[threadIdx.x >> 5];
-    uint32_t* cand = cand_all[threadIdx.x >> 5];
-    uint32_t kmin = 0xffffffffu, kmax = 0u;
-#pragma unroll
-    for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
-      if (key[e] != 0u) {
-        kmin = min(kmin, key[e]);
-        kmax = max(kmax, key[e]);
-      }
-    }
-    kmin = __reduce_min_sync(0xffffffffu, kmin);
-    kmax = __reduce_max_sync(0xffffffffu, kmax);
-    int shift = 32 - __clz(kmin ^ kmax);  // low bits that still vary across the row
-    uint32_t prefix = shift >= 32 ? 0u : (kmax & ~((1u << shift) - 1u));
-    need = k;
-    eqc = static_cast<uint32_t>(nk);  // every key is equal when no bit varies
-    if (shift > 0) {
-      radix_pass<PL>(key, h, lane, shift, prefix, need, eqc);
-      if (PL <= 48 && shift > 0 && eqc <= static_cast<uint32_t>(kCand)) {  // measured: no gain at 96 keys
-        const uint32_t lt = (1u << lane) - 1u;
-        int pos = 0;
-#pragma unroll
-        for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
-          const uint32_t u = key[e];
-          const bool m = u != 0u && (u >> shift) == (prefix >> shift);
-          const uint32_t mb = __ballot_sync(0xffffffffu, m);
-          if (m) cand[pos + __popc(mb & lt)] = u;
-          pos += __popc(mb);
-        }
-        __syncwarp();
-        uint32_t ck[kCand / 32];
-#pragma unroll
-        for (int c = 0; c < kCand / 32; ++c) ck[c] = lane + 32 * c < pos ? cand[lane + 32 * c] : 0u;
-        __syncwarp();
-        while (shift > 0) radix_pass<kCand / 32>(ck, h, lane, shift, prefix, need, eqc);
-      } else {
-        while (shift > 0) radix_pass<PL>(key, h, lane, shift, prefix, need, eqc);
-      }
-    }
-    T = prefix;
+    taken = select_emit<PL>(key, nk, k, lane, hist_all[threadIdx.x >> 5], cand_all[threadIdx.x >> 5], out);
   } else {
-    // rows too long for registers: binary search for the largest T with #(key >= T) >= k
-    // (every real key is >= 1), re-reading the row from memory
+    // binary search for the largest T with #(key >= T) >= k (every real key is >= 1)
+    auto count_ge = [&](uint32_t t) -> int {
+      int c = 0;
+      for (int j = lane; j < nk; j += 32) c += ordered_key(__ldg(src + j)) >= t ? 1 : 0;
+      return __reduce_add_sync(0xffffffffu, c);
+    };
     uint32_t lo = 1u, hi = 0xffffffffu;
     while (lo < hi) {
       const uint32_t mid = lo + ((hi - lo) >> 1) + 1u;
       if (count_ge(mid) >= k) lo = mid;
       else hi = mid - 1u;
     }
-    T = lo;
-    need = k - count_ge(T + (T != 0xffffffffu ? 1u : 0u)) * (T != 0xffffffffu ? 1 : 0);
-  }
-  int32_t* out = a.idx + static_cast<long long>(row) * k;
-  const uint32_t lt_mask = (1u << lane) - 1u;
-  int taken = 0, ties = 0;
-  auto emit = [&](uint32_t u, int j) {
-    const bool valid = j < nk;
-    const bool eq = valid && u == T;
-    const uint32_t eqb = __ballot_sync(0xffffffffu, eq);
-    const int rank = ties + __popc(eqb & lt_mask);
-    const bool sel = valid && (u > T || (eq && rank < need));
-    const uint32_t sb = __ballot_sync(0xffffffffu, sel);
-    if (sel) out[taken + __popc(sb & lt_mask)] = j;
-    taken += __popc(sb);
-    ties += __popc(eqb);
-  };
-  if (PL > 0 && need == static_cast<int>(eqc)) {
-    // every key equal to T is taken: one ballot per 32 keys
-#pragma unroll
-    for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
-      if (32 * e >= nk) break;  // warp-uniform
-      const int j = lane + 32 * e;
-      const bool sel = j < nk && key[e] >= T;
+    const uint32_t T = lo;
+    const int need = k - count_ge(T + (T != 0xffffffffu ? 1u : 0u)) * (T != 0xffffffffu ? 1 : 0);
+    const uint32_t lt_mask = (1u << lane) - 1u;
+    int ties = 0;
+    for (int j0 = 0; j0 < nk; j0 += 32) {
+      const int j = j0 + lane;
+      const uint32_t u = j < nk ? ordered_key(__ldg(src + j)) : 0u;
+      const bool valid = j < nk;
+      const bool eq = valid && u == T;
+      const uint32_t eqb = __ballot_sync(0xffffffffu, eq);
+      const int rank = ties + __popc(eqb & lt_mask);
+      const bool sel = valid && (u > T || (eq && rank < need));
       const uint32_t sb = __ballot_sync(0xffffffffu, sel);
       if (sel) out[taken + __popc(sb & lt_mask)] = j;
       taken += __popc(sb);
-    }
-  } else if (PL > 0) {
-#pragma unroll
-    for (int e = 0; e < (PL > 0 ? PL : 1); ++e) {
-      if (32 * e >= nk) break;  // warp-uniform
-      emit(key[e], lane + 32 * e);
-    }
-  } else {
-    for (int j0 = 0; j0 < nk; j0 += 32) {
-      const int j = j0 + lane;
-      emit(j < nk ? ordered_key(__ldg(src + j)) : 0u, j);
+      ties += __popc(eqb);
     }
   }
   if (lane == 0 && taken != k) atomicCAS(&g_score_err, 0, 201);

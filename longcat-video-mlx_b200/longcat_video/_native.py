@@ -45,6 +45,8 @@ _SIGNATURES = {
                        _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp], _i),
     "bsa_score_topk": ([_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp], _i),
     "bsa_block_scores": ([_vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
+    "bsa_route_scratch_bytes": ([_i, _i, _i], ctypes.c_int64),
+    "bsa_route_topk": ([_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp], _i),
     "bsa_topk_from_scores": ([_vp, _i, _i, _i, _vp, _vp], _i),
     "bsa_attention_indices": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i, _i,
                                _i, _i, _f, _vp, _c_i64p, _vp], _i),
@@ -209,7 +211,9 @@ def mean_pool(x: torch.Tensor, shape, chunk_thw, rope: Optional[Tuple] = None) -
 
 
 def score_topk(qp: torch.Tensor, kp: torch.Tensor, topk: int, return_scores: bool = False):
-    """Block scores + per-row top-k.  qp, kp: [B, H, nb, D] fp32 contiguous."""
+    """Block scores + per-row top-k.  qp, kp: [B, H, nb, D] fp32 contiguous.  Without ``return_scores``
+    the routing runs without materialising the score matrix (bsa_route_topk) where it supports the size;
+    both paths return the same indices."""
     _require_cuda(qp, kp)
     if qp.dtype != torch.float32 or kp.dtype != torch.float32:
         raise ValueError("pooled blocks must be fp32")
@@ -219,6 +223,13 @@ def score_topk(qp: torch.Tensor, kp: torch.Tensor, topk: int, return_scores: boo
     if kp.shape != qp.shape:
         raise ValueError("q and k block tensors must have the same shape for top-k routing")
     idx = torch.empty((B, H, nb, topk), device=qp.device, dtype=torch.int32)
+    nbytes = int(lib().bsa_route_scratch_bytes(B * H, nb, D)) if not return_scores else 0
+    if nbytes > 0:
+        scratch = torch.empty((nbytes,), device=qp.device, dtype=torch.uint8)
+        rc = lib().bsa_route_topk(qp.data_ptr(), kp.data_ptr(), B * H, nb, D, int(topk), idx.data_ptr(),
+                                  scratch.data_ptr(), _stream(qp))
+        _check(rc, "bsa_route_topk")
+        return idx, None
     scores = torch.empty((B, H, nb, nb), device=qp.device, dtype=torch.float32)  # GEMM output, top-k input
     rc = lib().bsa_score_topk(qp.data_ptr(), kp.data_ptr(), B * H, nb, D, int(topk), idx.data_ptr(),
                               scores.data_ptr(), _stream(qp))

@@ -59,8 +59,19 @@ def test_forward_scratch_size(lib):
     f = lib.bsa_forward_scratch_bytes
     f.restype = ctypes.c_int64
     f.argtypes = [ctypes.c_int] * 7
-    # pooled Q and K (2 x B*H x nb x D fp32) + the score matrix (B*H x nb x nb rounded to 4) at config 2
-    assert f(1, 32, 86400, 128, 1, 1, 64) == 2 * 32 * 1350 * 128 * 4 + 32 * 1350 * 1352 * 4
+    r = lib.bsa_route_scratch_bytes
+    r.restype = ctypes.c_int64
+    r.argtypes = [ctypes.c_int] * 3
+    up = lambda b: (b + 255) // 256 * 256
+    rows = 32 * 1350
+    # config 2: pooled Q and K (fp32), then the routing scratch: bf16 hi/lo pairs of both (128 columns),
+    # their norms, the per-head maximum key norm and the 16-bit score keys (rows padded to 8)
+    route = up(4 * rows * 128 * 2) + up(2 * rows * 4) + up(32 * 4) + up(rows * 1352 * 2)
+    assert r(32, 1350, 128) == route
+    assert f(1, 32, 86400, 128, 1, 1, 64) == up(2 * rows * 128 * 4) + route
+    # beyond 3,072 blocks per row the score matrix is used instead
+    assert r(1, 3073, 128) == 0
+    assert f(1, 1, 3073 * 64, 128, 1, 1, 64) == up(2 * 3073 * 128 * 4) + 3073 * 3076 * 4
 
 
 def _forward_args(lib, name):

@@ -100,6 +100,11 @@ def test_score_topk_bitexact(cuda, nb, D, k):
     assert _np(scores).tobytes() == ref_s.tobytes()
     ref_i, _ = orc.topk_block_indices(ref_s, topk=k)
     assert np.array_equal(idx.cpu().numpy(), ref_i)
+    # the same indices without the score matrix (tensor-core keys + exact scores near the threshold)
+    if nb <= 3072:
+        fused, _ = _native.score_topk(qp, kp, k)
+        assert _native.device_error(clear=True) == 0
+        assert np.array_equal(fused.cpu().numpy(), ref_i)
 
 
 def test_topk_from_scores_ties(cuda):
@@ -457,3 +462,46 @@ def test_misaligned_view_runs_the_engine(cuda):
     b, ib = bsa_attention(q.clone(), k.clone(), v.clone(), (8, 8, 8), chunk_thw=(4, 4, 4), topk=3,
                           return_indices=True)
     assert torch.equal(ia, ib) and torch.equal(a, b)
+
+
+def _route_vs_oracle(cuda, qp, kp, k):
+    from longcat_video import _native
+
+    got, _ = _native.score_topk(qp.to(cuda), kp.to(cuda), k)
+    assert _native.device_error(clear=True) == 0
+    ref, _ = orc.topk_block_indices(orc.block_routing_scores(_np(qp), _np(kp)), topk=k)
+    assert np.array_equal(got.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("nb,D,k", [(1, 128, 1), (7, 8, 3), (129, 40, 128), (1350, 128, 85), (1350, 128, 338),
+                                    (1536, 64, 1), (1537, 128, 700), (2700, 128, 169), (3072, 16, 3072)])
+def test_route_bitexact_sizes(cuda, nb, D, k):
+    """Routing without the score matrix equals the exact scores + top-k at every row-tile remainder, both
+    key-row widths (48 and 96 keys per lane), k = 1 and k = nb, and small head dims."""
+    g = torch.Generator().manual_seed(nb * 7 + D)
+    qp, kp = (torch.randn((1, 2, nb, D), generator=g) for _ in range(2))
+    _route_vs_oracle(cuda, qp, kp, k)
+
+
+def test_route_near_ties(cuda):
+    """Pooled i.i.d. fp16 blocks (the config-3 regime: scores crowd around the threshold): the band of
+    blocks scored exactly is dense, and the result is still exact."""
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn((2, 3, 1350, 64, 128), generator=g).half().float().mean(dim=3)
+    _route_vs_oracle(cuda, x[0].unsqueeze(0), x[1].unsqueeze(0), 169)
+
+
+def test_route_degenerate_rows_fall_back_to_exact(cuda):
+    """Rows the fast path cannot bound -- all scores tied, a non-finite or enormous key block, a zero query
+    block -- are scored exactly in full and still match the oracle."""
+    g = torch.Generator().manual_seed(12)
+    nb, D = 300, 64
+    qp = torch.randn((1, 4, nb, D), generator=g)
+    kp = torch.randn((1, 4, nb, D), generator=g)
+    kp[0, 0] = 1.0                      # head 0: every key block equal -> every score of a row tied
+    kp[0, 1, 17, 3] = 3.0e20            # head 1: one enormous key value (outside the norm bound's range)
+    qp[0, 2, 5] = 0.0                   # head 2: a zero query block (a row of zero scores)
+    qp[0, 3] = torch.round(qp[0, 3] * 4) / 4   # head 3: coarse values, many exact score ties
+    kp[0, 3] = torch.round(kp[0, 3] * 4) / 4
+    for k in (1, 30, 150):
+        _route_vs_oracle(cuda, qp, kp, k)
