@@ -11,7 +11,7 @@
 // An M = 64 accumulator occupies 16 of the 32 lanes of each TMEM lane quarter.  The two lane
 // halves (lanes 0-15 and 16-31 of every quarter) hold two independent pipelines over the same
 // columns: half 0 takes the even KV steps of a query block, half 1 the odd ones, each with its
-// own Q copy, S, P (three buffers) and O, and its own running max.  The epilogue merges the
+// own Q copy, S, P (double buffered) and O, and its own running max.  The epilogue merges the
 // two partial softmax states (m, l, O) of each row.
 //
 // Roles (384 threads, one CTA per SM, persistent over (head, q-block) units in head-major order so a
@@ -71,10 +71,8 @@ constexpr float kRescaleThreshold = 8.0f;           // log2 units: P <= 2^8 betw
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;                       // S: 128 fp32 columns
 constexpr uint32_t kColO = 128;                     // O: 128 fp32 columns
-constexpr int kPBufs = 3;                           // P buffers per lane half
-__host__ __device__ constexpr uint32_t col_p(int b) { return 256u + 64u * static_cast<uint32_t>(b); }  // P: 64 x 3
-constexpr uint32_t kColQ = 448;                     // Q: 64 columns (bf16/fp16 pairs)
-static_assert(kColQ == 256 + 64 * kPBufs && kColQ + 64 == 512, "TMEM columns");
+__host__ __device__ constexpr uint32_t col_p(int b) { return 256u + 64u * static_cast<uint32_t>(b); }  // P: 64 x 2
+constexpr uint32_t kColQ = 384;                     // Q: 64 columns (bf16/fp16 pairs)
 __host__ __device__ constexpr uint32_t half_lanes(int h) { return static_cast<uint32_t>(16 * h) << 16; }
 
 struct SmallSmem {
@@ -84,8 +82,8 @@ struct SmallSmem {
   uint64_t v_empty[kVSlots];
   uint64_t s_full[2];     // per half: QK issuer -> softmax, S ready
   uint64_t s_empty[2];    // per half: softmax -> QK issuer, S read (one arrival per warp of the half)
-  uint64_t p_full[2][kPBufs];  // [half][buf]: softmax -> PV issuer, P written (one arrival per warp)
-  uint64_t p_empty[2][kPBufs]; // [half][buf]: PV done (P buffer free, O of the half up to date)
+  uint64_t p_full[2][2];  // [half][buf]: softmax -> PV issuer, P written (one arrival per warp)
+  uint64_t p_empty[2][2]; // [half][buf]: PV done (P buffer free, O of the half up to date)
   uint64_t q_full[kQBufs];   // TMA: Q tile landed in shared memory
   uint64_t q_empty[kQBufs];  // softmax warps: Q tile copied into TMEM (shared buffer free)
   uint64_t q_ready[2];       // per half: Q of the unit is in TMEM (one arrival per warp of the half)
@@ -311,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ss.s_full[h], 1);
       mbar_init(&ss.s_empty[h], 4);
       mbar_init(&ss.q_ready[h], 4);
-      for (int b = 0; b < kPBufs; ++b) {
+      for (int b = 0; b < 2; ++b) {
         mbar_init(&ss.p_full[h][b], 4);
         mbar_init(&ss.p_empty[h][b], 1);
       }
@@ -487,22 +485,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ PV issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(64, 128, kBF16 ? 1 : 0, 0, 1);
-      RingPos<kPBufs> pp0, pp1;  // per half: P buffer of the next step and its fill phase
+      long long i0 = 0, i1 = 0;  // steps issued per half
       RingPos<kVSlots> vp;
       int n = 0;
       bool ok = true;
       for (int unit = blockIdx.x; unit < p.total_units && ok; unit += G, ++n) {
         for (int j = 0; j < nsteps && ok; ++j) {
           const int h = j & 1;
-          RingPos<kPBufs> pp = h ? pp1 : pp0;  // selected by value: the two halves' positions stay in registers
-          const int pb = pp.slot;
+          const long long i = h ? i1 : i0;  // step of the half
+          const int pb = static_cast<int>(i & 1);
           const int vs0 = vp.slot;
           ok = mbar_wait(&ss.v_full[vs0], vp.phase, abort_flag, err, 116, PACC(0));
           vp.next();
           const int vs1 = vp.slot;
           if (ok) ok = mbar_wait(&ss.v_full[vs1], vp.phase, abort_flag, err, 117, PACC(1));
           vp.next();
-          if (ok) ok = mbar_wait(&ss.p_full[h][pb], pp.phase, abort_flag, err, 111, PACC(2));
+          if (ok) ok = mbar_wait(&ss.p_full[h][pb], static_cast<uint32_t>((i >> 1) & 1), abort_flag, err, 111, PACC(2));
           if (ok && j == 0 && n >= 1) ok = mbar_wait(&ss.o_empty, static_cast<uint32_t>((n - 1) & 1), abort_flag, err, 112, PACC(3));
           if (!ok) break;
           tc_fence_after();
@@ -517,8 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&ss.v_empty[vs0]);
           umma_commit(&ss.v_empty[vs1]);
           umma_commit(&ss.p_empty[h][pb]);
-          pp.next();
-          if (h) pp1 = pp; else pp0 = pp;
+          if (h) ++i1; else ++i0;
         }
       }
       umma_commit(&ss.drain[1]);
@@ -539,7 +536,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool active = h == 0 || two_halves;    // half 1 has no steps when nsteps == 1
     const int hsteps = (nsteps + 1 - h) >> 1;    // steps of this half per unit
     long long i = 0;                             // steps of this half processed so far
-    RingPos<kPBufs> pbuf;                        // P buffer of step i and its fill phase
     int n = 0;
     bool ok = true;
 
@@ -600,8 +596,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool rescale = s > 0 && d != 0.f;
           if (__any_sync(0xffffffffu, rescale)) {
             // O rows of this half must be rescaled: the previous PV of this half must be complete
-            ok = mbar_wait(&ss.p_empty[h][pbuf.slot == 0 ? kPBufs - 1 : pbuf.slot - 1],
-                           pbuf.slot == 0 ? pbuf.phase ^ 1u : pbuf.phase, abort_flag, err, 122);
+            ok = mbar_wait(&ss.p_empty[h][(i - 1) & 1], static_cast<uint32_t>(((i - 1) >> 1) & 1), abort_flag, err,
+                           122);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
@@ -626,19 +622,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             packed[c] = pack2<kBF16>(p0, p1);
           }
           PTS(6);
-          if (i >= kPBufs) {  // the PV kPBufs steps back (same half) must be done reading this P buffer
-            ok = mbar_wait(&ss.p_empty[h][pbuf.slot], pbuf.phase ^ 1u, abort_flag, err, 124, PACC(1));
+          if (i >= 2) {  // the PV two steps back (same half) must be done reading this P buffer
+            ok = mbar_wait(&ss.p_empty[h][i & 1], static_cast<uint32_t>(((i - 2) >> 1) & 1), abort_flag, err, 124,
+                           PACC(1));
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
           }
           PTS_START();
-          tmem_st_16x2_x32(la + col_p(pbuf.slot), packed);
+          tmem_st_16x2_x32(la + col_p(static_cast<int>(i & 1)), packed);
           tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&ss.p_full[h][pbuf.slot]);
-          pbuf.next();
+          if (lane == 0) mbar_arrive(&ss.p_full[h][i & 1]);
           PTS(3);
         }
         if (!ok) break;
@@ -666,9 +662,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // carries the other half's.  Waiting on the other half's barrier here could run a whole phase
       // ahead of it (that half may still be two PVs behind), which a parity wait misreads as done.
       bool w = true;
-      if (active)  // the last step's P buffer and fill phase: one behind pbuf
-        w = mbar_wait(&ss.p_empty[h][pbuf.slot == 0 ? kPBufs - 1 : pbuf.slot - 1],
-                      pbuf.slot == 0 ? pbuf.phase ^ 1u : pbuf.phase, abort_flag, err, 125);
+      if (active) {
+        const long long last = i - 1;
+        w = mbar_wait(&ss.p_empty[h][last & 1], static_cast<uint32_t>((last >> 1) & 1), abort_flag, err, 125);
+      }
       __syncwarp();
       if (lane == 0 && w) mbar_arrive(&ss.ep[qq]);
       if (w) w = mbar_wait(&ss.ep[qq], static_cast<uint32_t>(n & 1), abort_flag, err, 127);

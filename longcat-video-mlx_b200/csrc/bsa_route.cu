@@ -247,8 +247,8 @@ __global__ void __launch_bounds__(kKeyThreads, 1)
 constexpr int kSelThreads = 256;
 struct SelWarp {
   uint32_t hist[256];
-  uint32_t cand[topk::kCand];
   float q[kDP];
+  uint32_t band_key[kMaxBand];  // exact scores of the band, order-preserving
   int32_t band_id[kMaxBand];
   uint8_t band_sel[kMaxBand];
 };
@@ -257,6 +257,9 @@ struct SelWarp {
 __device__ __forceinline__ float from_ordered(uint32_t o) {
   return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
 }
+// the fp32 interval a 16-bit key stands for
+__device__ __forceinline__ float key_low(uint32_t key) { return from_ordered(key << 16); }
+__device__ __forceinline__ float key_high(uint32_t key) { return from_ordered((key << 16) | 0xffffu); }
 
 // exact score: one fp32 fma chain over d = 0..D-1, starting at 0 (block_routing_scores, in the order
 // the CPU oracle uses)
@@ -300,32 +303,110 @@ __device__ __forceinline__ void exact_score2(const float* q, const float* __rest
   s1 = a1;
 }
 
-// Key thresholds of a band [L, U] with error bound e: keys >= *ks are above U (sure), finite keys
-// <= *ko are below L (out).  Both bounds are monotone in the key over the finite keys [0x80, 0xff80],
-// so each is a 16-step binary search.  Keys below 0x80 (NaN, -inf) are never sure nor out.
-__device__ __forceinline__ void band_keys(float L, float U, float e, uint32_t& ks, uint32_t& ko) {
-  uint32_t lo = 0x80u, hi = 0xff81u;  // smallest sure key in [lo, hi]; 0xff81: none
-  while (lo < hi) {
-    const uint32_t mid = (lo + hi) >> 1;
-    if (__fsub_rd(from_ordered(mid << 16), e) > U) hi = mid;
-    else lo = mid + 1u;
+// One byte of a radix select over the row's 16-bit keys (two per word; `valid` masks the keys past
+// nb): counts the byte `shift` of the keys whose bits above it equal `prefix`, then finds the value
+// of that byte holding the need-th largest key.  Updates prefix (the key bits found so far) and need.
+template <int NP>
+__device__ __forceinline__ void key_radix_byte(const uint32_t (&kw)[NP], int nb, uint32_t* h, int lane, int shift,
+                                               uint32_t& prefix, int& need) {
+  reinterpret_cast<uint4*>(h)[lane * 2] = make_uint4(0u, 0u, 0u, 0u);
+  reinterpret_cast<uint4*>(h)[lane * 2 + 1] = make_uint4(0u, 0u, 0u, 0u);
+  __syncwarp();
+  const uint32_t hi_mask = shift == 8 ? 0u : 0xff00u;  // bits above the counted byte that must match
+#pragma unroll
+  for (int e = 0; e < NP; ++e) {
+    const uint32_t w = kw[e];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t key = half ? (w >> 16) : (w & 0xffffu);
+      if (64 * e + 2 * lane + half < nb && (key & hi_mask) == (prefix & hi_mask))
+        atomicAdd(&h[(key >> shift) & 0xffu], 1u);
+    }
   }
-  ks = lo;
-  lo = 0x7fu;  // largest out key in [lo, hi]; 0x7f: none
-  hi = 0xff80u;
-  while (lo < hi) {
-    const uint32_t mid = (lo + hi + 1u) >> 1;
-    if (__fadd_ru(from_ordered((mid << 16) | 0xffffu), e) < L) lo = mid;
-    else hi = mid - 1u;
+  __syncwarp();
+  const uint4 c0 = reinterpret_cast<const uint4*>(h)[lane * 2];
+  const uint4 c1 = reinterpret_cast<const uint4*>(h)[lane * 2 + 1];
+  const uint32_t cnt[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  uint32_t tot = 0;
+#pragma unroll
+  for (int b = 0; b < 8; ++b) tot += cnt[b];
+  uint32_t suf = tot;  // inclusive suffix sum over lanes >= this lane
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t o = __shfl_down_sync(0xffffffffu, suf, off);
+    if (lane + off < 32) suf += o;
   }
-  ko = lo;
+  const uint32_t above = suf - tot;
+  const bool mine = above < static_cast<uint32_t>(need) && static_cast<uint32_t>(need) <= suf;
+  int digit = 0;
+  uint32_t gt = 0;
+  if (mine) {
+    uint32_t run = above;
+#pragma unroll
+    for (int b = 7; b >= 0; --b) {
+      if (run + cnt[b] >= static_cast<uint32_t>(need)) {
+        digit = lane * 8 + b;
+        gt = run;
+        break;
+      }
+      run += cnt[b];
+    }
+  }
+  const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+  digit = __shfl_sync(0xffffffffu, digit, src);
+  gt = __shfl_sync(0xffffffffu, gt, src);
+  prefix |= static_cast<uint32_t>(digit) << shift;
+  need -= static_cast<int>(gt);
+  __syncwarp();
 }
 
-template <int PL>
+// Smallest key whose interval minus e lies above U (keys at or above it are sure), and largest finite
+// key whose interval plus e lies below L (finite keys at or below it are out).  Both predicates are
+// monotone over the finite keys [0x80, 0xff80]; the 32 lanes probe 32 keys next to the k-th key at
+// once and a binary search covers the rare wider bands.
+__device__ __forceinline__ void band_keys(uint32_t T, float L, float U, float e, int lane, uint32_t& ks, uint32_t& ko) {
+  {
+    const uint32_t c = T + 1u + static_cast<uint32_t>(lane);
+    const bool p = c <= 0xff80u && __fsub_rd(key_low(c), e) > U;
+    const uint32_t b = __ballot_sync(0xffffffffu, p);
+    if (b) {
+      ks = T + 1u + static_cast<uint32_t>(__ffs(b) - 1);
+    } else {
+      uint32_t lo = T + 33u, hi = 0xff81u;  // 0xff81: no key is sure
+      if (lo > hi) lo = hi;
+      while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (__fsub_rd(key_low(mid), e) > U) hi = mid;
+        else lo = mid + 1u;
+      }
+      ks = lo;
+    }
+  }
+  {
+    const int c = static_cast<int>(T) - 1 - lane;
+    const bool p = c >= 0x80 && __fadd_ru(key_high(static_cast<uint32_t>(c)), e) < L;
+    const uint32_t b = __ballot_sync(0xffffffffu, p);
+    if (b) {
+      ko = T - 1u - static_cast<uint32_t>(__ffs(b) - 1);
+    } else {
+      int lo = 0x7f, hi = static_cast<int>(T) - 33;  // 0x7f: no key is out
+      if (hi < lo) hi = lo;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__fadd_ru(key_high(static_cast<uint32_t>(mid)), e) < L) lo = mid;
+        else hi = mid - 1;
+      }
+      ko = static_cast<uint32_t>(lo);
+    }
+  }
+}
+
+// NP words of two keys per lane: lane l holds keys 64e + 2l and 64e + 2l + 1 in word e (nb <= 64 NP).
+template <int NP>
 __global__ void __launch_bounds__(kSelThreads, 2)
     select_kernel(const uint16_t* __restrict__ keys, int ldk, const float* __restrict__ qp,
                   const float* __restrict__ kp, const float* __restrict__ nrm, const float* __restrict__ nkmax, int rows,
-                  int nb, int D, int k, int32_t* idx) {
+                  int nb, int D, int k, int32_t* idx, int* fb_count, int* fb_rows) {
   __shared__ SelWarp sw_all[kSelThreads / 32];
   const int lane = threadIdx.x & 31;
   SelWarp& sw = sw_all[threadIdx.x >> 5];
@@ -338,115 +419,139 @@ __global__ void __launch_bounds__(kSelThreads, 2)
       for (int j = lane; j < nb; j += 32) out[j] = j;
       continue;
     }
-    const float* kbase = kp + static_cast<long long>(bh) * nb * D;
-    // this row's q block, for the exact scores
     __syncwarp();
     for (int d = lane; d < D; d += 32) sw.q[d] = __ldg(qp + static_cast<long long>(row) * D + d);
-    const uint16_t* krow = keys + static_cast<long long>(row) * ldk;
-    uint32_t key[PL];
+    const uint32_t* krow = reinterpret_cast<const uint32_t*>(keys + static_cast<long long>(row) * ldk);
+    uint32_t kw[NP];  // word e: keys 64e + 2l (low half) and 64e + 2l + 1 (high half); validity is j < nb
 #pragma unroll
-    for (int e = 0; e < PL; ++e) {
-      const int j = lane + 32 * e;
-      key[e] = j < nb ? static_cast<uint32_t>(__ldg(krow + j)) : 0u;
-    }
+    for (int e = 0; e < NP; ++e) kw[e] = 64 * e + 2 * lane < nb ? __ldg(krow + 32 * e + lane) : 0u;
     const float ebound = __fmul_ru(__fmul_ru(kErrC, __ldg(nrm + row)), __ldg(nkmax + bh));
-    int need;
-    uint32_t eqc;
-    const uint32_t T = topk::kth_largest<PL>(key, nb, k, lane, sw.hist, sw.cand, need, eqc);
-    // s_(k) in [L, U]; a key's interval is [from_ordered(key << 16), from_ordered(key << 16 | 0xffff)]
-    const float L = __fsub_rd(from_ordered(T << 16), ebound);
-    const float U = __fadd_ru(from_ordered((T << 16) | 0xffffu), ebound);
-    uint32_t ks, ko;
-    band_keys(L, U, ebound, ks, ko);
-    // key classes: sure (key >= ks), out (0x80 <= key <= ko), band (the rest of the valid keys)
-    auto is_sure = [&](uint32_t u) { return u >= ks; };
-    auto is_band = [&](uint32_t u) { return u != 0u && u < ks && (u > ko || u < 0x80u); };
-    int n_sure = 0, n_band = 0;
+    // the k-th largest key T: high byte, then low byte
+    uint32_t T = 0;
+    int need = k;
+    key_radix_byte<NP>(kw, nb, sw.hist, lane, 8, T, need);
+    key_radix_byte<NP>(kw, nb, sw.hist, lane, 0, T, need);
+    // s_(k) in [L, U]
+    const float L = __fsub_rd(key_low(T), ebound);
+    const float U = __fadd_ru(key_high(T), ebound);
+    uint32_t ks = 0xff81u, ko = 0x7fu;
+    if (ebound < INFINITY) band_keys(T, L, U, ebound, lane, ks, ko);
+    // classes: sure (key >= ks), out (0x80 <= key <= ko), band (the other valid keys); band ids ascending
+    int n_sure = 0, pos = 0;
 #pragma unroll
-    for (int e = 0; e < PL; ++e) {
-      n_sure += __popc(__ballot_sync(0xffffffffu, is_sure(key[e])));
-      n_band += __popc(__ballot_sync(0xffffffffu, is_band(key[e])));
+    for (int e = 0; e < NP; ++e) {
+      const uint32_t k0 = kw[e] & 0xffffu, k1 = kw[e] >> 16;
+      const bool v0 = 64 * e + 2 * lane < nb, v1 = 64 * e + 2 * lane + 1 < nb;
+      n_sure += (v0 && k0 >= ks) + (v1 && k1 >= ks);
+      const bool b0 = v0 && k0 < ks && (k0 > ko || k0 < 0x80u);
+      const bool b1 = v1 && k1 < ks && (k1 > ko || k1 < 0x80u);
+      const uint32_t m0 = __ballot_sync(0xffffffffu, b0), m1 = __ballot_sync(0xffffffffu, b1);
+      const int p0 = pos + __popc(m0 & lt) + __popc(m1 & lt);
+      if (b0 && p0 < kMaxBand) sw.band_id[p0] = 64 * e + 2 * lane;
+      if (b1 && p0 + b0 < kMaxBand) sw.band_id[p0 + b0] = 64 * e + 2 * lane + 1;
+      pos += __popc(m0) + __popc(m1);
     }
+    n_sure = __reduce_add_sync(0xffffffffu, n_sure);
+    const int n_band = pos;
     const bool fast = ebound < INFINITY && n_band <= kMaxBand && n_sure <= k && n_sure + n_band >= k;
-    int taken = 0;
+    if (!fast) {  // scored exactly in full by fallback_kernel
+      if (lane == 0) fb_rows[atomicAdd(fb_count, 1)] = row;
+      continue;
+    }
     __syncwarp();
-    if (fast) {
-      // the band's block ids, ascending
-      int pos = 0;
+    // exact scores of the band (two per lane at most)
+    const float* kbase = kp + static_cast<long long>(bh) * nb * D;
+    if (lane < n_band) {
+      float s0, s1;
+      const float* r1 = lane + 32 < n_band ? kbase + static_cast<long long>(sw.band_id[lane + 32]) * D : nullptr;
+      exact_score2(sw.q, kbase + static_cast<long long>(sw.band_id[lane]) * D, r1, D, s0, s1);
+      sw.band_key[lane] = topk::ordered_key(s0);
+      if (r1) sw.band_key[lane + 32] = topk::ordered_key(s1);
+    }
+    __syncwarp();
+    // the `rest` largest of the band, ties to the smaller id: rank by comparison (the band is short)
+    const int rest = k - n_sure;
 #pragma unroll
-      for (int e = 0; e < PL; ++e) {
-        const bool band = is_band(key[e]);
-        const uint32_t bb = __ballot_sync(0xffffffffu, band);
-        if (band) sw.band_id[pos + __popc(bb & lt)] = lane + 32 * e;
-        pos += __popc(bb);
-      }
-      __syncwarp();
-      // exact scores of the band (two per lane at most), as order-preserving keys
-      uint32_t ek[2] = {0u, 0u};
-      if (lane < n_band) {
-        float s0, s1;
-        const float* r1 = lane + 32 < n_band ? kbase + static_cast<long long>(sw.band_id[lane + 32]) * D : nullptr;
-        exact_score2(sw.q, kbase + static_cast<long long>(sw.band_id[lane]) * D, r1, D, s0, s1);
-        ek[0] = topk::ordered_key(s0);
-        if (r1) ek[1] = topk::ordered_key(s1);
-      }
-      // the `rest` largest of the band (ties to the smaller id): binary search for the threshold key
-      const int rest = k - n_sure;
-      auto count_ge = [&](uint32_t t) -> int {
-        return __reduce_add_sync(0xffffffffu, (ek[0] >= t ? 1 : 0) + (ek[1] >= t ? 1 : 0));
-      };
-      uint32_t T2 = 0xffffffffu;
-      int take_eq = 0;
-      if (rest > 0) {
-        uint32_t lo = 1u, hi = 0xffffffffu;
-        while (lo < hi) {
-          const uint32_t mid = lo + ((hi - lo) >> 1) + 1u;
-          if (count_ge(mid) >= rest) lo = mid;
-          else hi = mid - 1u;
+    for (int t = 0; t < 2; ++t) {
+      const int b = lane + 32 * t;
+      if (b < n_band) {
+        const uint32_t mk = sw.band_key[b];
+        int rank = 0;
+        for (int u = 0; u < n_band; ++u) {
+          const uint32_t o = sw.band_key[u];
+          rank += (o > mk || (o == mk && u < b)) ? 1 : 0;
         }
-        T2 = lo;
-        take_eq = rest - (T2 != 0xffffffffu ? count_ge(T2 + 1u) : 0);
+        sw.band_sel[b] = rank < rest;
       }
-      const bool eq0 = rest > 0 && ek[0] == T2, eq1 = rest > 0 && ek[1] == T2;
-      const uint32_t b0 = __ballot_sync(0xffffffffu, eq0), b1 = __ballot_sync(0xffffffffu, eq1);
-      const int r0 = __popc(b0 & lt), r1 = __popc(b0) + __popc(b1 & lt);
-      if (lane < n_band) sw.band_sel[lane] = rest > 0 && (ek[0] > T2 || (eq0 && r0 < take_eq));
-      if (lane + 32 < n_band) sw.band_sel[lane + 32] = rest > 0 && (ek[1] > T2 || (eq1 && r1 < take_eq));
-      __syncwarp();
-      // ascending emission: sure blocks and the chosen band blocks
-      int bpos = 0;
+    }
+    __syncwarp();
+    // ascending emission: sure blocks and the chosen band blocks
+    int taken = 0, bpos = 0;
 #pragma unroll
-      for (int e = 0; e < PL; ++e) {
-        if (32 * e >= nb) break;  // warp-uniform
-        const uint32_t u = key[e];
-        const bool band = is_band(u);
-        const uint32_t bb = __ballot_sync(0xffffffffu, band);
-        const bool sel = is_sure(u) || (band && sw.band_sel[bpos + __popc(bb & lt)]);
-        const uint32_t sb = __ballot_sync(0xffffffffu, sel);
-        if (sel) out[taken + __popc(sb & lt)] = lane + 32 * e;
-        taken += __popc(sb);
-        bpos += __popc(bb);
-      }
-    } else {
-      // the whole row scored exactly, then the same selection as the top-k kernel
-#pragma unroll
-      for (int e = 0; e < PL; ++e) {
-        const int j = lane + 32 * e;
-        key[e] = j < nb ? topk::ordered_key(exact_score(sw.q, kbase + static_cast<long long>(j) * D, D)) : 0u;
-      }
-      taken = topk::select_emit<PL>(key, nb, k, lane, sw.hist, sw.cand, out);
+    for (int e = 0; e < NP; ++e) {
+      if (64 * e >= nb) break;  // warp-uniform
+      const uint32_t k0 = kw[e] & 0xffffu, k1 = kw[e] >> 16;
+      const bool v0 = 64 * e + 2 * lane < nb, v1 = 64 * e + 2 * lane + 1 < nb;
+      const bool b0 = v0 && k0 < ks && (k0 > ko || k0 < 0x80u);
+      const bool b1 = v1 && k1 < ks && (k1 > ko || k1 < 0x80u);
+      const uint32_t m0 = __ballot_sync(0xffffffffu, b0), m1 = __ballot_sync(0xffffffffu, b1);
+      const int p0 = bpos + __popc(m0 & lt) + __popc(m1 & lt);
+      const bool s0 = (v0 && k0 >= ks) || (b0 && sw.band_sel[p0]);
+      const bool s1 = (v1 && k1 >= ks) || (b1 && sw.band_sel[p0 + b0]);
+      const uint32_t t0 = __ballot_sync(0xffffffffu, s0), t1 = __ballot_sync(0xffffffffu, s1);
+      const int q0 = taken + __popc(t0 & lt) + __popc(t1 & lt);
+      if (s0) out[q0] = 64 * e + 2 * lane;
+      if (s1) out[q0 + s0] = 64 * e + 2 * lane + 1;
+      taken += __popc(t0) + __popc(t1);
+      bpos += __popc(m0) + __popc(m1);
     }
     if (lane == 0 && taken != k) atomicCAS(&g_route_err, 0, 410);
   }
 }
 
+// Rows the fast path could not bound: every score exact (one warp per row), then the register radix
+// select of the top-k kernel.  The row list comes from select_kernel.
+template <int PL>
+__global__ void __launch_bounds__(kSelThreads, 2)
+    fallback_kernel(const float* __restrict__ qp, const float* __restrict__ kp, int nb, int D, int k, int32_t* idx,
+                    const int* fb_count, const int* fb_rows) {
+  __shared__ __align__(16) uint32_t hist_all[kSelThreads / 32][256];
+  __shared__ uint32_t cand_all[kSelThreads / 32][topk::kCand];
+  __shared__ float q_all[kSelThreads / 32][kDP];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int n = *fb_count;
+  for (int i = blockIdx.x * (kSelThreads / 32) + w; i < n; i += gridDim.x * (kSelThreads / 32)) {
+    const int row = fb_rows[i];
+    const int bh = row / nb;
+    __syncwarp();
+    for (int d = lane; d < D; d += 32) q_all[w][d] = __ldg(qp + static_cast<long long>(row) * D + d);
+    __syncwarp();
+    const float* kbase = kp + static_cast<long long>(bh) * nb * D;
+    uint32_t key[PL];
+#pragma unroll
+    for (int e = 0; e < PL; ++e) {
+      const int j = lane + 32 * e;
+      key[e] = j < nb ? topk::ordered_key(exact_score(q_all[w], kbase + static_cast<long long>(j) * D, D)) : 0u;
+    }
+    const int taken = topk::select_emit<PL>(key, nb, k, lane, hist_all[w], cand_all[w],
+                                            idx + static_cast<long long>(row) * k);
+    if (lane == 0 && taken != k) atomicCAS(&g_route_err, 0, 411);
+  }
+}
+
 }  // namespace route
+
+// Scratch layout: bf16 pairs [4][rows][128] | norms [2][rows] | per-head max key norm [BH] and the
+// fallback row count (zeroed together) | fallback row list [rows] | keys [rows][round_up(nb, 8)].
+namespace {
+int64_t up256(int64_t b) { return (b + 255) & ~int64_t(255); }
+}  // namespace
 
 int64_t route_scratch_bytes(int BH, int nb) {
   const int64_t rows = static_cast<int64_t>(BH) * nb;
   const int64_t ldk = (static_cast<int64_t>(nb) + 7) & ~int64_t(7);
-  auto up = [](int64_t b) { return (b + 255) & ~int64_t(255); };
-  return up(4 * rows * route::kDP * 2) + up(2 * rows * 4) + up(static_cast<int64_t>(BH) * 4) + up(rows * ldk * 2);
+  return up256(4 * rows * route::kDP * 2) + up256(2 * rows * 4) + up256((static_cast<int64_t>(BH) + 4) * 4) +
+         up256(rows * 4) + up256(rows * ldk * 2);
 }
 
 bool route_supported(int nb, int D) { return nb >= 1 && nb <= 3072 && D >= 8 && D <= 128 && D % 8 == 0; }
@@ -456,20 +561,22 @@ int launch_route(const RouteArgs& a, cudaStream_t stream) {
   if (!route_supported(a.nb, a.D) || !a.scratch) return BSA_ERR_SHAPE;
   const int rows = a.BH * a.nb;
   const int64_t ldk = (static_cast<int64_t>(a.nb) + 7) & ~int64_t(7);
-  auto up = [](int64_t b) { return (b + 255) & ~int64_t(255); };
   uint8_t* base = static_cast<uint8_t*>(a.scratch);
   __nv_bfloat16* hl = reinterpret_cast<__nv_bfloat16*>(base);
-  base += up(4ll * rows * kDP * 2);
+  base += up256(4ll * rows * kDP * 2);
   float* nrm = reinterpret_cast<float*>(base);
-  base += up(2ll * rows * 4);
+  base += up256(2ll * rows * 4);
   float* nkmax = reinterpret_cast<float*>(base);
-  base += up(static_cast<int64_t>(a.BH) * 4);
+  int* fb_count = reinterpret_cast<int*>(nkmax + a.BH);
+  base += up256((static_cast<int64_t>(a.BH) + 4) * 4);
+  int* fb_rows = reinterpret_cast<int*>(base);
+  base += up256(static_cast<int64_t>(rows) * 4);
   uint16_t* keys = reinterpret_cast<uint16_t*>(base);
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return BSA_ERR_CUDA;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // 1. split (+ the per-head maximum key norm, which starts at 0)
-  if (cudaMemsetAsync(nkmax, 0, static_cast<size_t>(a.BH) * 4, stream) != cudaSuccess) return BSA_ERR_CUDA;
+  // 1. split (+ the per-head maximum key norm and the fallback count, which start at 0)
+  if (cudaMemsetAsync(nkmax, 0, (static_cast<size_t>(a.BH) + 4) * 4, stream) != cudaSuccess) return BSA_ERR_CUDA;
   {
     long long grid = (2ll * rows + 7) / 8;
     if (grid > static_cast<long long>(sms) * 16) grid = static_cast<long long>(sms) * 16;
@@ -497,16 +604,20 @@ int launch_route(const RouteArgs& a, cudaStream_t stream) {
     key_kernel<<<grid, kKeyThreads, kKeySmemBytes, stream>>>(maps[0], maps[1], maps[2], maps[3], a.nb,
                                                              static_cast<int>(ldk), keys);
   }
-  // 3. select
+  // 3. select, then the exact full-row path for the rows the band could not settle
   {
     long long grid = (static_cast<long long>(rows) + 7) / 8;
-    if (grid > static_cast<long long>(sms) * 8) grid = static_cast<long long>(sms) * 8;
-    if (a.nb <= 32 * 48)
+    if (grid > static_cast<long long>(sms) * 12) grid = static_cast<long long>(sms) * 12;
+    const unsigned fgrid = static_cast<unsigned>(sms) * 2;
+    if (a.nb <= 64 * 24) {
+      select_kernel<24><<<static_cast<unsigned>(grid), kSelThreads, 0, stream>>>(
+          keys, static_cast<int>(ldk), a.qp, a.kp, nrm, nkmax, rows, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
+      fallback_kernel<48><<<fgrid, kSelThreads, 0, stream>>>(a.qp, a.kp, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
+    } else {
       select_kernel<48><<<static_cast<unsigned>(grid), kSelThreads, 0, stream>>>(
-          keys, static_cast<int>(ldk), a.qp, a.kp, nrm, nkmax, rows, a.nb, a.D, a.topk, a.idx);
-    else
-      select_kernel<96><<<static_cast<unsigned>(grid), kSelThreads, 0, stream>>>(
-          keys, static_cast<int>(ldk), a.qp, a.kp, nrm, nkmax, rows, a.nb, a.D, a.topk, a.idx);
+          keys, static_cast<int>(ldk), a.qp, a.kp, nrm, nkmax, rows, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
+      fallback_kernel<96><<<fgrid, kSelThreads, 0, stream>>>(a.qp, a.kp, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
+    }
   }
   return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
 }

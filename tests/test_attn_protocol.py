@@ -46,7 +46,7 @@ def wait(bar, phase):
     return bar.completed == phase + 1
 
 
-def run_protocol(units, nsteps, kstages, vslots, qbufs, seed, rescale_prob=0.2, pbufs=3):
+def run_protocol(units, nsteps, kstages, vslots, qbufs, seed, rescale_prob=0.2):
     rng = random.Random(seed)
     two_halves = nsteps >= 2
     copy_warps = 8 if two_halves else 4
@@ -61,7 +61,7 @@ def run_protocol(units, nsteps, kstages, vslots, qbufs, seed, rescale_prob=0.2, 
         bar(("v_full", s)); bar(("v_empty", s))
     for h in range(2):
         bar(("s_full", h)); bar(("s_empty", h), 4); bar(("q_ready", h), 4)
-        for b in range(pbufs):
+        for b in range(2):
             bar(("p_full", h, b), 4); bar(("p_empty", h, b))
     for b in range(qbufs):
         bar(("q_full", b)); bar(("q_empty", b), copy_warps)
@@ -136,14 +136,14 @@ def run_protocol(units, nsteps, kstages, vslots, qbufs, seed, rescale_prob=0.2, 
                     gb = 2 * g + bi
                     while not wait(B[("v_full", gb % vslots)], gb // vslots):
                         yield
-                while not wait(B[("p_full", h, i % pbufs)], i // pbufs):
+                while not wait(B[("p_full", h, i & 1)], i >> 1):
                     yield
                 if j == 0 and n >= 1:
                     while not wait(B[("o_empty",)], n - 1):
                         yield
                 async_q["mma_pv"].append(("v_empty", (2 * g) % vslots))
                 async_q["mma_pv"].append(("v_empty", (2 * g + 1) % vslots))
-                async_q["mma_pv"].append(("p_empty", h, i % pbufs))
+                async_q["mma_pv"].append(("p_empty", h, i & 1))
                 cnt[h] += 1
                 g += 1
                 yield
@@ -169,19 +169,19 @@ def run_protocol(units, nsteps, kstages, vslots, qbufs, seed, rescale_prob=0.2, 
                     B[("s_empty", h)].arrive()
                     yield
                     if s > 0 and rng.random() < rescale_prob:  # the lazy max moved: O of this half is rescaled
-                        while not wait(B[("p_empty", h, (i - 1) % pbufs)], (i - 1) // pbufs):
+                        while not wait(B[("p_empty", h, (i - 1) & 1)], (i - 1) >> 1):
                             yield
-                    if i >= pbufs:
-                        while not wait(B[("p_empty", h, i % pbufs)], (i - pbufs) // pbufs):
+                    if i >= 2:
+                        while not wait(B[("p_empty", h, i & 1)], (i - 2) >> 1):
                             yield
-                    B[("p_full", h, i % pbufs)].arrive()
+                    B[("p_full", h, i & 1)].arrive()
                     i += 1
                     yield
                 if n + 1 < units:
                     yield from copy_q(n + 1)
             if active:  # this half's last PV of the unit; the ep handshake carries the other half's
                 last = i - 1
-                while not wait(B[("p_empty", h, last % pbufs)], last // pbufs):
+                while not wait(B[("p_empty", h, last & 1)], last >> 1):
                     yield
             B[("ep", qq)].arrive()
             while not wait(B[("ep", qq)], n):
@@ -189,7 +189,7 @@ def run_protocol(units, nsteps, kstages, vslots, qbufs, seed, rescale_prob=0.2, 
             # O is read here: every PV of this unit, in both halves, must have completed
             for hh in ((0, 1) if two_halves else (0,)):
                 lh = (n + 1) * hs[hh] - 1
-                assert B[("p_empty", hh, lh % pbufs)].completed >= lh // pbufs + 1, ("O read early", n, hh)
+                assert B[("p_empty", hh, lh & 1)].completed >= (lh >> 1) + 1, ("O read early", n, hh)
             B[("o_empty",)].arrive()
             yield
 
@@ -223,10 +223,9 @@ def run_protocol(units, nsteps, kstages, vslots, qbufs, seed, rescale_prob=0.2, 
 @pytest.mark.parametrize("nsteps", [1, 2, 3, 4, 43])
 @pytest.mark.parametrize("units", [1, 2, 5])
 @pytest.mark.parametrize("rings", [(2, 8, 2), (3, 6, 2), (2, 9, 1), (4, 4, 2)])
-@pytest.mark.parametrize("pbufs", [3, 2])
-def test_attention_barrier_protocol(nsteps, units, rings, pbufs):
+def test_attention_barrier_protocol(nsteps, units, rings):
     for seed in range(6 if nsteps < 43 else 2):
-        run_protocol(units, nsteps, *rings, seed=seed, pbufs=pbufs)
+        run_protocol(units, nsteps, *rings, seed=seed)
 
 
 def test_protocol_model_detects_aliasing():

@@ -65,8 +65,9 @@ def test_forward_scratch_size(lib):
     up = lambda b: (b + 255) // 256 * 256
     rows = 32 * 1350
     # config 2: pooled Q and K (fp32), then the routing scratch: bf16 hi/lo pairs of both (128 columns),
-    # their norms, the per-head maximum key norm and the 16-bit score keys (rows padded to 8)
-    route = up(4 * rows * 128 * 2) + up(2 * rows * 4) + up(32 * 4) + up(rows * 1352 * 2)
+    # their norms, the per-head maximum key norm (+ a counter), the fallback row list and the 16-bit
+    # score keys (rows padded to 8)
+    route = up(4 * rows * 128 * 2) + up(2 * rows * 4) + up((32 + 4) * 4) + up(rows * 4) + up(rows * 1352 * 2)
     assert r(32, 1350, 128) == route
     assert f(1, 32, 86400, 128, 1, 1, 64) == up(2 * rows * 128 * 4) + route
     # beyond 3,072 blocks per row the score matrix is used instead
