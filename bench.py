@@ -4,7 +4,9 @@ TFLOP/s = 4*B*H*S*k*64*D / t, as a fraction of bf16 tensor peak).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config config2] [--impl ours|reference]
 
 One step = one full BSA call on synthetic config inputs already resident in HBM: Q and K block
-pooling, the fp32 block-score GEMM, top-k and the sparse tcgen05 attention (5 kernel launches).
+pooling, routing (bf16 pair split, tcgen05 approximate score keys, per-row selection with exact fp32
+scores in the threshold band, the exact fallback for unsettled rows) and the sparse tcgen05 attention
+(7 kernel launches).
 At N > 1 (torchrun, one rank per GPU, NCCL) every rank holds a sequence shard of Q/K/V for all
 32 heads; a step is the sequence -> heads exchange, the BSA call on its 32/N heads and the
 exchange back, pipelined over head groups (ulysses_bsa_attention).
@@ -36,12 +38,16 @@ for _p in (REPO, PKG):
 
 METRIC = "BSA sparse TFLOP/s (4*B*H*S*k*64*D per call) at the 720p refinement shape"
 UNIT = "TFLOP/s"
-# DRAM bytes (read + write) of one attention launch per (batch, head) at the config-2 shape, from the ncu
-# capture summarised in profiles/bsa_kernels_config2_h4_full.md (401 MB for 4 heads; traffic is per head).
-ATTN_DRAM_BYTES_PER_HEAD = {"config2": (319.036672e6 + 81.871872e6) / 4}
-# L2 -> SM rate of TMA gathers of 16 KB K/V blocks measured alone on this part (working sets of 8-100 MB): the
-# ceiling of the attention kernel's tile gather.
-TMA_GATHER_CEILING_TBS = 11.0
+# DRAM bytes (read + write) of one attention launch per (batch, head) at the config-2 shape: ncu
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch on 4 heads of config 2 (inputs 265 MB, above
+# the L2), 316.7 + 77.0 MB; the traffic is per head.
+ATTN_DRAM_BYTES_PER_HEAD = {"config2": (316.661504e6 + 77.043968e6) / 4}
+# L2 -> shared-memory rate of TMA tensor gathers alone: 148 CTAs, each keeping 192 KB of random 16 KB K+V
+# blocks (two 64 x 64 bf16 boxes each, 128B swizzle) of one head's 44 MB working set in flight and
+# releasing every block as it lands; 13.1-14.7 TB/s on two boxes, whatever the map's rank (2-D, 3-D or
+# 5-D).  Plain loads go faster (1-D bulk copies 18.6, LDG.128 20.2 TB/s) but cannot produce the swizzled
+# operand layout the MMA reads.  The ceiling of the attention kernel's K/V gather.
+TMA_GATHER_CEILING_TBS = 13.4
 
 
 def attn_gather_bytes(cfg, world: int = 1) -> float:
@@ -374,6 +380,24 @@ def run_ours(args, cfg):
     ms_per_step = total_ms / args.steps
     value = cfg.sparse_flops() / (ms_per_step * 1e-3) / 1e12
 
+    # ---- host time per call of the library path: the Python API down to the C ABI (argument checks,
+    # tensor maps, launches), enqueue only; the GPU runs behind
+    host_us = None
+    if world == 1:
+        scratch = torch.empty((int(_native.lib().bsa_forward_scratch_bytes(B, cfg.H, S, D, *cfg.chunk)),),
+                              device=dev, dtype=torch.uint8)
+        fwd = lambda: _native.forward(q, k, v, cfg.shape, cfg.chunk, cfg.topk, scale, rope=rope_args, out=out_h,
+                                      block_indices=idx, scratch=scratch)
+        fwd()
+        torch.cuda.synchronize()
+        n_host = 20
+        th0 = time.perf_counter()
+        for _ in range(n_host):
+            fwd()
+        host_us = (time.perf_counter() - th0) / n_host * 1e6
+        torch.cuda.synchronize()
+        del scratch
+
     # ---- end to end through the public API with host buffers (pinned), per rank
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
@@ -441,22 +465,22 @@ def run_ours(args, cfg):
                        "exchange": args.exchange if world > 1 else None,
                        "l2": "inputs 2.1 GB > 126 MB L2, no flush"},
             "pct_bf16_peak": value / peak_tf,
-            "kernel_ms": {"routing(pool+score+topk)": route_avg, "attention": attn_avg},
+            "kernel_ms": {"routing(pool+route)": route_avg, "attention": attn_avg},
+            "host_us_per_call": host_us,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "traffic": traffic, "peak_kind": f"{peak_kind} bf16 burst",
                          "frac_of_sustained": achieved / peak_tf_sus, "kernel": "bsa_attn_kernel",
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, 4-head capture "
-                                           "scaled per head (profiles/bsa_kernels_config2_h4_full.md)"
-                         if traffic else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch on 4 "
+                                           "heads of config 2, scaled per head" if traffic else None,
                          # the resource the kernel actually runs against: the K/V tile gather from L2
                          "gather": {"unit": "TB/s", "bytes": gbytes, "achieved": gbytes / (attn_avg * 1e-3) / 1e12,
                                     "ceiling": TMA_GATHER_CEILING_TBS,
                                     "frac": gbytes / (attn_avg * 1e-3) / 1e12 / TMA_GATHER_CEILING_TBS,
-                                    "ceiling_kind": "measured TMA gather of 16 KB blocks from L2"}},
+                                    "ceiling_kind": "measured TMA tensor gather of 16 KB K+V blocks from L2 alone"}},
             "e2e": {"value": cfg.sparse_flops() / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            # per step: pool Q, pool K, score GEMM, top-k, attention
-            "gpu_launches": 5 * args.steps,
+            # per step: pool Q, pool K, pair split, score keys, select, fallback, attention
+            "gpu_launches": 7 * args.steps,
             "clocks": clk.summary(),
         }
         if cpu:

@@ -68,6 +68,17 @@ int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t 
                   int T, int Hl, int Wl, int cT, int cH, int cW, const float* rope, int rope_dt, int rope_dh,
                   int rope_dw, int rope_T, int rope_H, int rope_W, void* x_rot, float* pooled, void* stream);
 
+/* bsa_mean_pool with the q/k RMSNorm of the DiT attention fused in front of the RoPE --
+ * RMSNorm_FP32 (longcat_video/models/blocks.py:55-73) applied as attention.py:195-196 does, then
+ * rope_3d.py:107-128, then block_sparse_attention.py:67-104.  Per token row: x * rsqrt(mean(x^2) + eps) in
+ * fp32 (the sum of squares in a fixed order; rsqrt to within its hardware error), rounded to the input
+ * dtype, times norm_weight (input dtype, [D], 16-byte aligned) rounded again; then the optional RoPE.
+ * The transformed rows are written to x_rot (required) and pooled. */
+int bsa_mean_pool_norm(const void* x, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss,
+                       int T, int Hl, int Wl, int cT, int cH, int cW, const float* rope, int rope_dt, int rope_dh,
+                       int rope_dw, int rope_T, int rope_H, int rope_W, const void* norm_weight, float norm_eps,
+                       void* x_rot, float* pooled, void* stream);
+
 /* block_routing_scores + topk_block_indices -- block_sparse_attention.py:107-134.
  * score[i][j] = fp32 fma chain over d = 0..D-1 of q_pooled[i][d] * k_pooled[j][d]; each row
  * keeps the topk largest scores (ties: smaller block id first) and writes their block ids
@@ -136,6 +147,17 @@ int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B
                    int rope_dh, int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot,
                    void* scratch, int32_t* block_indices, void* out, const int64_t* out_strides, int sm_reserve,
                    void* stream);
+
+/* bsa_forward_ex on the raw q/k of the attention's QKV projection: the q/k RMSNorm
+ * (attention.py:195-196, blocks.py:55-73; q_norm_weight / k_norm_weight in the input dtype, [D]) runs
+ * fused with the optional RoPE and the pooling (bsa_mean_pool_norm), q_rot / k_rot receive the
+ * normalised (and rotated) tensors, and the attention reads them. */
+int bsa_forward_qknorm(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
+                       const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl,
+                       int Wl, int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt,
+                       int rope_dh, int rope_dw, int rope_T, int rope_H, int rope_W, const void* q_norm_weight,
+                       const void* k_norm_weight, float norm_eps, void* q_rot, void* k_rot, void* scratch,
+                       int32_t* block_indices, void* out, const int64_t* out_strides, int sm_reserve, void* stream);
 
 /* bsa_forward without caller-provided scratch -- no counterpart in the reference (MLX manages
  * memory itself); it exists for callers that cannot allocate device memory where they call

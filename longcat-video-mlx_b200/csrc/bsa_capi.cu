@@ -142,7 +142,8 @@ struct PoolPlan {
 
 int pool_plan(PoolPlan& pl, const void* x, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss,
               int T, int Hl, int Wl, int cT, int cH, int cW, const float* rope, int rope_dt, int rope_dh, int rope_dw,
-              int rope_T, int rope_H, int rope_W, void* x_rot, float* pooled) {
+              int rope_T, int rope_H, int rope_W, void* x_rot, float* pooled, const void* norm_w = nullptr,
+              float norm_eps = 0.f) {
   if (!x || !pooled) return fail(BSA_ERR_ARG, "null pointer");
   if (dtype != BSA_DTYPE_F32 && dtype != BSA_DTYPE_F16 && dtype != BSA_DTYPE_BF16)
     return fail(BSA_ERR_DTYPE, "unsupported dtype code %d", dtype);
@@ -156,6 +157,12 @@ int pool_plan(PoolPlan& pl, const void* x, int dtype, int B, int H, int S, int D
   if (!aligned16(x) || (ss * e) % 16 || (sh * e) % 16 || (sb * e) % 16)
     return fail(BSA_ERR_ALIGN, "x must be 16-byte aligned with 16-byte-multiple strides");
   if (!aligned16(pooled)) return fail(BSA_ERR_ALIGN, "pooled must be 16-byte aligned");
+  if (norm_w) {
+    if (!x_rot) return fail(BSA_ERR_ARG, "x_rot is required with a norm weight");
+    if (!aligned16(norm_w)) return fail(BSA_ERR_ALIGN, "the norm weight must be 16-byte aligned");
+    if (!(norm_eps >= 0.f)) return fail(BSA_ERR_ARG, "norm eps must be >= 0");
+    if (!aligned16(x_rot)) return fail(BSA_ERR_ALIGN, "x_rot must be 16-byte aligned");
+  }
   if (rope) {
     if (!x_rot) return fail(BSA_ERR_ARG, "x_rot is required with rope tables");
     if (!aligned16(x_rot)) return fail(BSA_ERR_ALIGN, "x_rot must be 16-byte aligned");
@@ -171,12 +178,13 @@ int pool_plan(PoolPlan& pl, const void* x, int dtype, int B, int H, int S, int D
   a.rope = rope; a.rope_dt = rope_dt; a.rope_dh = rope_dh; a.rope_dw = rope_dw;
   a.rope_T = rope_T; a.rope_H = rope_H; a.rope_W = rope_W;
   a.x_rot = x_rot; a.pooled = pooled;
+  a.norm_w = norm_w; a.norm_eps = norm_eps;
   a.tmap = nullptr;
   a.map3 = 0;
   pl.has_map = false;
   // bf16/fp16 blocks of 64 d-wide halves stream through a TMA ring; the map needs mergeable batch
   // and head strides, which the register kernel does not
-  if (dtype != BSA_DTYPE_F32 && !rope && (B == 1 || sb == static_cast<int64_t>(H) * sh)) {
+  if (dtype != BSA_DTYPE_F32 && !rope && !norm_w && (B == 1 || sb == static_cast<int64_t>(H) * sh)) {
     // a map that cannot be built only selects the register kernel: keep the caller's last message
     char saved[sizeof(g_msg)];
     memcpy(saved, g_msg, sizeof(g_msg));
@@ -279,6 +287,18 @@ int bsa_mean_pool(const void* x, int dtype, int B, int H, int S, int D, int64_t 
   PoolPlan pl;
   const int rc = pool_plan(pl, x, dtype, B, H, S, D, sb, sh, ss, T, Hl, Wl, cT, cH, cW, rope, rope_dt, rope_dh,
                            rope_dw, rope_T, rope_H, rope_W, x_rot, pooled);
+  if (rc) return rc;
+  return pool_run(pl, stream);
+}
+
+int bsa_mean_pool_norm(const void* x, int dtype, int B, int H, int S, int D, int64_t sb, int64_t sh, int64_t ss, int T,
+                       int Hl, int Wl, int cT, int cH, int cW, const float* rope, int rope_dt, int rope_dh,
+                       int rope_dw, int rope_T, int rope_H, int rope_W, const void* norm_weight, float norm_eps,
+                       void* x_rot, float* pooled, void* stream) {
+  if (!norm_weight) return fail(BSA_ERR_ARG, "null pointer");
+  PoolPlan pl;
+  const int rc = pool_plan(pl, x, dtype, B, H, S, D, sb, sh, ss, T, Hl, Wl, cT, cH, cW, rope, rope_dt, rope_dh,
+                           rope_dw, rope_T, rope_H, rope_W, x_rot, pooled, norm_weight, norm_eps);
   if (rc) return rc;
   return pool_run(pl, stream);
 }
@@ -392,12 +412,15 @@ int bsa_forward(const void* q, const void* k, const void* v, int dtype, int B, i
                         block_indices, out, out_strides, 0, stream);
 }
 
-int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
-                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl,
-                   int Wl, int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt,
-                   int rope_dh, int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot,
-                   void* scratch, int32_t* block_indices, void* out, const int64_t* out_strides, int sm_reserve,
-                   void* stream) {
+}  // extern "C"
+
+namespace {
+int forward_impl(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
+                 const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl, int Wl,
+                 int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt, int rope_dh,
+                 int rope_dw, int rope_T, int rope_H, int rope_W, const void* q_norm_w, const void* k_norm_w,
+                 float norm_eps, void* q_rot, void* k_rot, void* scratch, int32_t* block_indices, void* out,
+                 const int64_t* out_strides, int sm_reserve, void* stream) {
   // ---- every check first: nothing is queued unless the whole call is valid
   if (sm_reserve < 0) return fail(BSA_ERR_ARG, "sm_reserve=%d must be >= 0", sm_reserve);
   if (!q || !k || !v || !scratch || !block_indices || !out || !q_strides || !k_strides || !v_strides || !out_strides)
@@ -415,12 +438,13 @@ int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B
   if (topk < 1 || topk > nb) return fail(BSA_ERR_SHAPE, "topk=%d out of range for %d KV blocks", topk, nb);
   float* qp = static_cast<float*>(scratch);
   float* kp = qp + static_cast<int64_t>(B) * H * nb * D;
+  if ((q_norm_w != nullptr) != (k_norm_w != nullptr)) return fail(BSA_ERR_ARG, "q and k norm weights come together");
   PoolPlan pq, pk;
   if ((rc = pool_plan(pq, q, dtype, B, H, S, D, q_strides[0], q_strides[1], q_strides[2], T, Hl, Wl, cT, cH, cW, rope,
-                      rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, q_rot, qp)))
+                      rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, q_rot, qp, q_norm_w, norm_eps)))
     return rc;
   if ((rc = pool_plan(pk, k, dtype, B, H, S, D, k_strides[0], k_strides[1], k_strides[2], T, Hl, Wl, cT, cH, cW, rope,
-                      rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, k_rot, kp)))
+                      rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, k_rot, kp, k_norm_w, norm_eps)))
     return rc;
   void* rest = static_cast<uint8_t*>(scratch) + ((2ll * B * H * nb * D * 4 + 255) & ~int64_t(255));
   const bool route = bsa::route_supported(nb, D);
@@ -432,8 +456,8 @@ int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B
   sa.idx = block_indices; sa.ldc = static_cast<int>(score_ld(nb));
   sa.scores = static_cast<float*>(rest);
   AttnPlan pa;
-  if (rope) {
-    // the attention reads the rotated tensors the pool kernels write (contiguous [B,H,S,D])
+  if (rope || q_norm_w) {
+    // the attention reads the transformed tensors the pool kernels write (contiguous [B,H,S,D])
     const int64_t cst[3] = {static_cast<int64_t>(H) * S * D, static_cast<int64_t>(S) * D, D};
     rc = attn_plan(pa, q_rot, k_rot, v, block_indices, dtype, B, H, S, D, cst, cst, v_strides, T, Hl, Wl, cT, cH, cW,
                    topk, sm_scale, out, out_strides, sm_reserve);
@@ -450,6 +474,32 @@ int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B
   if (rc == BSA_ERR_CUDA) return cuda_fail("routing kernel launch");
   if (rc) return rc == BSA_ERR_ARG ? rc : fail(rc, "routing: unsupported sizes (nb=%d)", nb);
   return attn_run(pa, stream);
+}
+}  // namespace
+
+extern "C" {
+
+int bsa_forward_ex(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
+                   const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl,
+                   int Wl, int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt,
+                   int rope_dh, int rope_dw, int rope_T, int rope_H, int rope_W, void* q_rot, void* k_rot,
+                   void* scratch, int32_t* block_indices, void* out, const int64_t* out_strides, int sm_reserve,
+                   void* stream) {
+  return forward_impl(q, k, v, dtype, B, H, S, D, q_strides, k_strides, v_strides, T, Hl, Wl, cT, cH, cW, topk,
+                      sm_scale, rope, rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, nullptr, nullptr, 0.f, q_rot,
+                      k_rot, scratch, block_indices, out, out_strides, sm_reserve, stream);
+}
+
+int bsa_forward_qknorm(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
+                       const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl,
+                       int Wl, int cT, int cH, int cW, int topk, float sm_scale, const float* rope, int rope_dt,
+                       int rope_dh, int rope_dw, int rope_T, int rope_H, int rope_W, const void* q_norm_weight,
+                       const void* k_norm_weight, float norm_eps, void* q_rot, void* k_rot, void* scratch,
+                       int32_t* block_indices, void* out, const int64_t* out_strides, int sm_reserve, void* stream) {
+  if (!q_norm_weight || !k_norm_weight) return fail(BSA_ERR_ARG, "null pointer");
+  return forward_impl(q, k, v, dtype, B, H, S, D, q_strides, k_strides, v_strides, T, Hl, Wl, cT, cH, cW, topk,
+                      sm_scale, rope, rope_dt, rope_dh, rope_dw, rope_T, rope_H, rope_W, q_norm_weight, k_norm_weight,
+                      norm_eps, q_rot, k_rot, scratch, block_indices, out, out_strides, sm_reserve, stream);
 }
 
 }  // extern "C"

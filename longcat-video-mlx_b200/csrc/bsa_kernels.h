@@ -22,6 +22,9 @@ struct PoolArgs {
   float* pooled;         // [B*H, nb, D] fp32
   const CUtensorMap* tmap;  // nullable: block map over x (bf16/fp16); selects the TMA-ring kernel
   int map3;                 // tmap is 3-D (d, s, b*h) (contiguous blocks), else 5-D (d, w, h, t, b*h)
+  // optional fused RMSNorm_FP32 (blocks.py:55-73) before the RoPE: weight [D] in x's dtype (nullable)
+  const void* norm_w;
+  float norm_eps;
 };
 int launch_pool(const PoolArgs& a, cudaStream_t stream);
 

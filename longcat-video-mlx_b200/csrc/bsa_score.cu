@@ -45,6 +45,8 @@ struct Geo {
   const float* rope;
   int rdt, rdh, rdw, rT, rH, rW;
   int map3;  // the TMA-ring kernel's map is 3-D (d, s, b*h): blocks are contiguous token runs
+  const void* nw;  // nullable: RMSNorm weight [D] in the input dtype (fused q/k norm)
+  float eps;
 };
 
 // Four consecutive d values of one token row: 8 bytes (fp16/bf16) or 16 bytes (fp32).
@@ -110,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, kRope ? 3 : 4)
   const float* rcos[2] = {nullptr, nullptr};
   const float* rsin[2] = {nullptr, nullptr};
   int rstride[2] = {0, 0}, rax[2] = {0, 0};
-  if (kRope) {
+  if (kRope && g.rope) {
     const int ht = g.rdt >> 1, hh2 = g.rdh >> 1, hw2 = g.rdw >> 1;
     const float* tab_t = g.rope;
     const float* tab_h = tab_t + 2 * g.rT * ht;
@@ -141,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, kRope ? 3 : 4)
     // RoPE grid positions of rows `lane` and `lane + 32` (token s at t = s / (H*W), h = (s / W) % H,
     // w = s % W), packed as (t) and (h << 16 | w) and handed to the other lanes by shuffle
     int posA0 = 0, posB0 = 0, posA1 = 0, posB1 = 0;
-    if (kRope) {
+    if (kRope && g.rope) {
       const int rhw = g.rH * g.rW;
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
@@ -171,26 +173,46 @@ __global__ void __launch_bounds__(kThreads, kRope ? 3 : 4)
         const int r = r0 + i;
         if (r >= g.n) break;
         if (kRope) {
-          // this row's position on the RoPE grid, computed by lane r % 32 at the start of the block
-          const int src = r & 31;
-          const int pt = __shfl_sync(0xffffffffu, r < 32 ? posA0 : posA1, src);
-          const int pb = __shfl_sync(0xffffffffu, r < 32 ? posB0 : posB1, src);
-          const int pax[3] = {pt, pb >> 16, pb & 0xffff};
-          if (dact) {
-            // rotate 2 pairs: (x0, x1) -> (x0*cos - x1*sin, x1*cos + x0*sin), fp32, no fma
+          // the row's transform, written to x_rot and pooled from there: optional RMSNorm_FP32
+          // (blocks.py:55-73), then optional 3-D RoPE (rope_3d.py:120-128)
+          if (g.nw) {
+            // fp32 mean of squares: each lane ((v0^2 + v1^2) + (v2^2 + v3^2)), then a butterfly over
+            // the lanes (every lane ends with the same sum); lanes past D hold zeros
+            float ss = __fadd_rn(__fadd_rn(__fmul_rn(v[i][0], v[i][0]), __fmul_rn(v[i][1], v[i][1])),
+                                 __fadd_rn(__fmul_rn(v[i][2], v[i][2]), __fmul_rn(v[i][3], v[i][3])));
 #pragma unroll
-            for (int pr = 0; pr < 2; ++pr) {
-              const int pos = pax[rax[pr]];
-              const float cs = __ldg(rcos[pr] + pos * rstride[pr]);
-              const float sn = __ldg(rsin[pr] + pos * rstride[pr]);
-              const float a = v[i][2 * pr], bb = v[i][2 * pr + 1];
-              v[i][2 * pr] = __fadd_rn(__fmul_rn(a, cs), __fmul_rn(-bb, sn));
-              v[i][2 * pr + 1] = __fadd_rn(__fmul_rn(bb, cs), __fmul_rn(a, sn));
+            for (int off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
+            const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(g.D)), g.eps));
+            if (dact) {
+              float wv[4];
+              load4(static_cast<const T*>(g.nw) + d0, wv);
+              // x * rsqrt in fp32, cast to the input dtype, times the weight in the input dtype
+#pragma unroll
+              for (int e = 0; e < 4; ++e) v[i][e] = round_to(__fmul_rn(round_to(__fmul_rn(v[i][e], rs), x), wv[e]), x);
             }
-#pragma unroll
-            for (int e = 0; e < 4; ++e) v[i][e] = round_to(v[i][e], x);
-            store4(xr + (static_cast<long long>(bh) * g.S + tok0 + roff[r]) * g.D + d0, v[i]);
           }
+          if (g.rope) {
+            // this row's position on the RoPE grid, computed by lane r % 32 at the start of the block
+            const int src = r & 31;
+            const int pt = __shfl_sync(0xffffffffu, r < 32 ? posA0 : posA1, src);
+            const int pb = __shfl_sync(0xffffffffu, r < 32 ? posB0 : posB1, src);
+            const int pax[3] = {pt, pb >> 16, pb & 0xffff};
+            if (dact) {
+              // rotate 2 pairs: (x0, x1) -> (x0*cos - x1*sin, x1*cos + x0*sin), fp32, no fma
+#pragma unroll
+              for (int pr = 0; pr < 2; ++pr) {
+                const int pos = pax[rax[pr]];
+                const float cs = __ldg(rcos[pr] + pos * rstride[pr]);
+                const float sn = __ldg(rsin[pr] + pos * rstride[pr]);
+                const float a = v[i][2 * pr], bb = v[i][2 * pr + 1];
+                v[i][2 * pr] = __fadd_rn(__fmul_rn(a, cs), __fmul_rn(-bb, sn));
+                v[i][2 * pr + 1] = __fadd_rn(__fmul_rn(bb, cs), __fmul_rn(a, sn));
+              }
+#pragma unroll
+              for (int e = 0; e < 4; ++e) v[i][e] = round_to(v[i][e], x);
+            }
+          }
+          if (dact) store4(xr + (static_cast<long long>(bh) * g.S + tok0 + roff[r]) * g.D + d0, v[i]);
         }
         // insert row r into the binary counter: merge with every complete run that ends at r
         float c[4] = {v[i][0], v[i][1], v[i][2], v[i][3]};
@@ -418,6 +440,7 @@ int launch_pool(const PoolArgs& a, cudaStream_t stream) {
   g.rope = a.rope; g.rdt = a.rope_dt; g.rdh = a.rope_dh; g.rdw = a.rope_dw;
   g.rT = a.rope_T; g.rH = a.rope_H; g.rW = a.rope_W;
   g.map3 = a.map3;
+  g.nw = a.norm_w; g.eps = a.norm_eps;
   if (n < 1 || n > 64 || (n & (n - 1)) || a.D > 128 || a.D % 4) return BSA_ERR_SHAPE;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
@@ -428,7 +451,7 @@ int launch_pool(const PoolArgs& a, cudaStream_t stream) {
   if (grid > need) grid = need;
   if (grid < 1) return BSA_OK;
   dim3 gd(static_cast<unsigned>(grid), 1, 1);
-  const bool rope = a.rope != nullptr;
+  const bool rope = a.rope != nullptr || a.norm_w != nullptr;  // a transform: the register kernel writes x_rot
   if (a.tmap && !rope && (a.dtype == BSA_DTYPE_BF16 || a.dtype == BSA_DTYPE_F16)) {
     // TMA ring: one persistent CTA per SM.  With fused RoPE the register kernel stays faster (its 32
     // warps per SM hide the per-row table loads and the rotated-row stores; 1.77 vs 2.22 ms of routing)

@@ -62,6 +62,11 @@ _SIGNATURES = {
                                   _i, _i, _i, _f, _vp, _c_i64p, _i, _vp], _i),
     "bsa_forward_ex": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i, _i, _i, _i, _f,
                         _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _c_i64p, _i, _vp], _i),
+    "bsa_mean_pool_norm": ([_vp, _i, _i, _i, _i, _i, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _i, _i, _i, _i,
+                            _i, _i, _vp, _i, _i, _i, _i, _i, _i, _vp, _f, _vp, _vp, _vp], _i),
+    "bsa_forward_qknorm": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i, _i, _i, _i,
+                            _f, _vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _f, _vp, _vp, _vp, _vp, _vp, _c_i64p, _i, _vp],
+                           _i),
 }
 
 
@@ -186,8 +191,18 @@ def _geometry(S: int, shape: Sequence[int], chunk_thw: Sequence[int]):
 
 
 # ------------------------------------------------------------------------------------ ops
-def mean_pool(x: torch.Tensor, shape, chunk_thw, rope: Optional[Tuple] = None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
-    """fp32 block means [B, H, nb, D]; with ``rope=(tables, dims, grid)`` also the rotated x."""
+def _norm_weight(w: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+    """An RMSNorm weight as the kernels read it: [D], the input's dtype and device, contiguous."""
+    w = w.detach().to(device=like.device, dtype=like.dtype).contiguous()
+    if w.dim() != 1 or w.numel() != like.shape[-1]:
+        raise ValueError(f"norm weight must be [{like.shape[-1]}]")
+    return w
+
+
+def mean_pool(x: torch.Tensor, shape, chunk_thw, rope: Optional[Tuple] = None,
+              norm: Optional[Tuple[torch.Tensor, float]] = None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """fp32 block means [B, H, nb, D]; with ``rope=(tables, dims, grid)`` and / or ``norm=(weight, eps)``
+    (the DiT's q/k RMSNorm, fused before the RoPE) also the transformed x."""
     _require_cuda(x)
     if x.dim() != 4:
         raise ValueError("expected x of shape [B, H, S, D]")
@@ -201,8 +216,16 @@ def mean_pool(x: torch.Tensor, shape, chunk_thw, rope: Optional[Tuple] = None) -
     rope_ptr, rdims, rgrid = None, (0, 0, 0), (0, 0, 0)
     if rope is not None:
         tables, rdims, rgrid = rope
-        x_rot = torch.empty((B, H, S, D), device=x.device, dtype=x.dtype)
         rope_ptr = tables.data_ptr()
+    if rope is not None or norm is not None:
+        x_rot = torch.empty((B, H, S, D), device=x.device, dtype=x.dtype)
+    if norm is not None:
+        w = _norm_weight(norm[0], x)
+        rc = lib().bsa_mean_pool_norm(x.data_ptr(), _dtype_code(x), B, H, S, D, st[0], st[1], st[2], T, H_, W, cT, cH,
+                                      cW, rope_ptr, rdims[0], rdims[1], rdims[2], rgrid[0], rgrid[1], rgrid[2],
+                                      w.data_ptr(), float(norm[1]), x_rot.data_ptr(), pooled.data_ptr(), _stream(x))
+        _check(rc, "bsa_mean_pool_norm")
+        return pooled, x_rot
     rc = lib().bsa_mean_pool(x.data_ptr(), _dtype_code(x), B, H, S, D, st[0], st[1], st[2], T, H_, W, cT, cH, cW,
                              rope_ptr, rdims[0], rdims[1], rdims[2], rgrid[0], rgrid[1], rgrid[2],
                              x_rot.data_ptr() if x_rot is not None else None, pooled.data_ptr(), _stream(x))
@@ -337,9 +360,12 @@ def _attention_ex(q, k, v, bi, shape, chunk_thw, sm_scale, out, sm_reserve):
 
 def forward(q, k, v, shape, chunk_thw, topk: int, sm_scale: float, rope: Optional[Tuple] = None,
             out: Optional[torch.Tensor] = None, block_indices: Optional[torch.Tensor] = None,
-            scratch: Optional[torch.Tensor] = None, sm_reserve: int = 0):
+            scratch: Optional[torch.Tensor] = None, sm_reserve: int = 0,
+            qk_norm: Optional[Tuple[torch.Tensor, torch.Tensor, float]] = None):
     """Full BSA call (pool -> score -> top-k -> sparse attention).  Returns (out, block_indices).
-    ``sm_reserve`` SMs stay free of the persistent attention kernel (for a concurrent exchange)."""
+    ``sm_reserve`` SMs stay free of the persistent attention kernel (for a concurrent exchange).
+    ``qk_norm=(q_weight, k_weight, eps)``: q and k are the raw projections; their RMSNorm runs fused
+    with the RoPE and the pooling (bsa_forward_qknorm)."""
     _require_cuda(q, k, v)
     if q.shape != k.shape or q.shape != v.shape:
         raise ValueError("q, k, v must have the same shape [B, H, S, D]")
@@ -349,6 +375,8 @@ def forward(q, k, v, shape, chunk_thw, topk: int, sm_scale: float, rope: Optiona
     T, H_, W, cT, cH, cW = _geometry(S, shape, chunk_thw)
     nb = S // (cT * cH * cW)
     if q.dtype == torch.float32:
+        if qk_norm is not None:
+            raise ValueError("the fused q/k norm runs on bf16 / fp16 inputs")
         return _forward_f32(q, k, v, shape, chunk_thw, topk, sm_scale, rope, out, block_indices, sm_reserve)
     q, k, v = _merge_batch(q), _merge_batch(k), _merge_batch(v)
     if out is None:
@@ -363,8 +391,19 @@ def forward(q, k, v, shape, chunk_thw, topk: int, sm_scale: float, rope: Optiona
     if rope is not None:
         tables, rdims, rgrid = rope
         rope_ptr = tables.data_ptr()
+    if rope is not None or qk_norm is not None:
         q_rot = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
         k_rot = torch.empty((B, H, S, D), device=q.device, dtype=q.dtype)
+    if qk_norm is not None:
+        wq, wk = _norm_weight(qk_norm[0], q), _norm_weight(qk_norm[1], k)
+        rc = lib().bsa_forward_qknorm(q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype_code(q), B, H, S, D,
+                                      _strides(q), _strides(k), _strides(v), T, H_, W, cT, cH, cW, int(topk),
+                                      float(sm_scale), rope_ptr, rdims[0], rdims[1], rdims[2], rgrid[0], rgrid[1],
+                                      rgrid[2], wq.data_ptr(), wk.data_ptr(), float(qk_norm[2]), q_rot.data_ptr(),
+                                      k_rot.data_ptr(), scratch.data_ptr(), block_indices.data_ptr(), out.data_ptr(),
+                                      _strides(out), int(sm_reserve), _stream(q))
+        _check(rc, "bsa_forward_qknorm")
+        return out, block_indices
     rc = lib().bsa_forward_ex(q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype_code(q), B, H, S, D, _strides(q),
                            _strides(k), _strides(v), T, H_, W, cT, cH, cW, int(topk), float(sm_scale), rope_ptr,
                            rdims[0], rdims[1], rdims[2], rgrid[0], rgrid[1], rgrid[2],

@@ -2,7 +2,9 @@
 ``longcat_video/models/attention.py:35-275``), in torch, with the hook routed to the B200 engine.
 
 Only what the BSA path needs is here: QKV projection, fp32 RMSNorm on q/k (blocks.py:55-73),
-3-D RoPE, ``_process_attn`` (the hook, :71-179) and the output projection.  Every BSA backend
+3-D RoPE, ``_process_attn`` (the hook, :71-179) and the output projection.  On the BSA path the q/k
+RMSNorm and the RoPE run fused in the engine's routing kernel, and the engine writes its output in the
+[B, N, H, D] order the projection reads.  Every BSA backend
 name the reference accepts routes to the one CUDA engine; the hook's own fallback -- a
 shape that is not a multiple of chunk_thw falls back to dense attention (:174-179) -- is kept as
 the reference has it, and only for that error.  With BSA on, RoPE is fused into the routing
@@ -61,15 +63,21 @@ class Attention(torch.nn.Module):
         return self.enable_bsa and shape is not None and q.shape[-2] == k.shape[-2]
 
     def _process_attn(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                      shape: Optional[Tuple[int, int, int]] = None, rope_grid=None) -> torch.Tensor:
+                      shape: Optional[Tuple[int, int, int]] = None, rope_grid=None,
+                      out: Optional[torch.Tensor] = None, raw_qk: bool = False) -> torch.Tensor:
         """attention.py:71-179.  q, k, v: [B, H, S, D].  With ``rope_grid`` set, q and k are
-        pre-RoPE: the BSA path fuses the rotation, the dense path applies it first."""
+        pre-RoPE: the BSA path fuses the rotation, the dense path applies it first.  With ``raw_qk``
+        they are also pre-RMSNorm (attention.py:195-196): the BSA path fuses q_norm / k_norm in front of
+        the rotation, the dense path applies them first.  ``out`` (device tensors only): a
+        [B, H, S, D] view the BSA path writes in place -- any strides, e.g. a permuted [B, S, H, D]
+        buffer; the dense path ignores it."""
         if self._bsa_ok(q, k, shape):
             try:
                 rope = self.rope_3d.tables(rope_grid, q.device) if rope_grid is not None else None
+                qk_norm = (self.q_norm.weight, self.k_norm.weight, self.q_norm.eps) if raw_qk else None
                 return bsa_attention(q, k, v, shape=shape, sparsity=self.bsa_sparsity,
                                      chunk_thw=self.bsa_chunk_thw, sm_scale=self.scale, topk=self.bsa_topk,
-                                     rope=rope)
+                                     rope=rope, out=out, qk_norm=qk_norm)
             except BSAShapeError:
                 # shape not a multiple of chunk_thw: the reference falls back to dense attention
                 # here (attention.py:174-179).  Every other engine error (unsupported head_dim or
@@ -77,6 +85,8 @@ class Attention(torch.nn.Module):
                 # FLOPs with no message.  Views the kernels cannot read in place are copied once by
                 # the engine's host layer, not refused.
                 pass
+        if raw_qk:
+            q, k = self.q_norm(q), self.k_norm(k)
         if rope_grid is not None:
             q, k = self.rope_3d(q, k, rope_grid)
         return F.scaled_dot_product_attention(q, k, v, scale=self.scale)
@@ -88,8 +98,14 @@ class Attention(torch.nn.Module):
         B, N, C = x.shape
         qkv = self.qkv(x).reshape(B, N, 3, self.num_heads, self.head_dim).permute(2, 0, 3, 1, 4)
         q, k, v = qkv[0], qkv[1], qkv[2]
-        q = self.q_norm(q)
-        k = self.k_norm(k)
+        # the q/k RMSNorm runs fused in the engine's routing kernel (one read of the raw q/k, one write of
+        # the normalised, rotated q/k) when the call takes the BSA path on the GPU in bf16/fp16
+        fuse_norm = (not return_kv and not (num_cond_latents is not None and num_cond_latents > 0)
+                     and self._bsa_ok(q, k, shape) and q.is_cuda and q.dtype in (torch.bfloat16, torch.float16)
+                     and self.q_norm.eps == self.k_norm.eps)
+        if not fuse_norm:
+            q = self.q_norm(q)
+            k = self.k_norm(k)
         kv = (k, v) if return_kv else None
         if num_cond_latents is not None and num_cond_latents > 0:
             q, k = self.rope_3d(q, k, shape)
@@ -99,7 +115,17 @@ class Attention(torch.nn.Module):
             x_noise = self._process_attn(q[:, :, ncl:], k, v, shape=None)
             out = torch.cat([x_cond, x_noise], dim=2)
         else:
-            out = self._process_attn(q, k, v, shape=shape, rope_grid=shape)
+            # the engine writes straight into a [B, N, H, D] buffer (attention.py:228-229 transposes to
+            # it), so proj reads the result without a transpose copy
+            o_nhd = None
+            if self.enable_bsa and q.is_cuda:
+                o_nhd = torch.empty((B, N, self.num_heads, self.head_dim), device=q.device, dtype=q.dtype)
+            out = self._process_attn(q, k, v, shape=shape, rope_grid=shape,
+                                     out=o_nhd.permute(0, 2, 1, 3) if o_nhd is not None else None,
+                                     raw_qk=fuse_norm)
+            if o_nhd is not None and out.data_ptr() == o_nhd.data_ptr():
+                out = self.proj(o_nhd.view(B, N, C))
+                return (out, kv) if return_kv else out
         out = self.proj(out.transpose(1, 2).reshape(B, N, C))
         return (out, kv) if return_kv else out
 

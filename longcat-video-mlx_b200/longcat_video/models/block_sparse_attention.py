@@ -98,7 +98,8 @@ def build_token_pair_mask(block_indices: torch.Tensor, token_block_index: torch.
 def bsa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, shape: Tuple[int, int, int],
                   sparsity: float = 0.9375, chunk_thw: Tuple[int, int, int] = (4, 4, 4),
                   sm_scale: Optional[float] = None, *, topk: Optional[int] = None, rope=None,
-                  return_indices: bool = False, sm_reserve: int = 0, out: Optional[torch.Tensor] = None):
+                  return_indices: bool = False, sm_reserve: int = 0, out: Optional[torch.Tensor] = None,
+                  qk_norm=None):
     """block_sparse_attention.py:201-250 (Tier A entry) on the CUDA engine.
 
     q, k, v: [B, H, S, D] (bf16 or fp16, d contiguous), S = T*H*W, 64-token blocks.  CUDA tensors
@@ -110,6 +111,8 @@ def bsa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, shape: Tupl
     sm_reserve: SMs kept free of the persistent attention kernel, for kernels of a concurrent
     exchange on other streams (device tensors only).
     out: optional preallocated [B, H, S, D] output on q's device (device tensors only).
+    qk_norm: optional ``(q_weight, k_weight, eps)`` (device tensors only): q and k are the raw projections
+    and their RMSNorm_FP32 (blocks.py:55-73) runs fused with the RoPE and the pooling.
     Returns [B, H, S, D] (and the [B, H, nb, k] routing when ``return_indices``).
     """
     if sm_scale is None:
@@ -120,12 +123,12 @@ def bsa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, shape: Tupl
     k_sel = num_selected_blocks(nb, sparsity) if topk is None else int(topk)
     rope_arg = rope.native_args() if rope is not None else None
     if not q.is_cuda and not k.is_cuda and not v.is_cuda:
-        if out is not None:
-            raise ValueError("out= is for device tensors")
+        if out is not None or qk_norm is not None:
+            raise ValueError("out= and qk_norm= are for device tensors")
         out, idx = _forward_host_streamed(q, k, v, shape, chunk_thw, k_sel, sm_scale, rope_arg, return_indices)
     else:
         out, idx = _native.forward(q, k, v, shape, chunk_thw, k_sel, sm_scale, rope=rope_arg, sm_reserve=sm_reserve,
-                                   out=out)
+                                   out=out, qk_norm=qk_norm)
     return (out, idx) if return_indices else out
 
 

@@ -59,6 +59,20 @@ class LongCatVideoTransformer3DModel(torch.nn.Module):
             block.attn.bsa_chunk_thw = self._bsa_chunk_thw
             block.attn.bsa_backend = backend
             block.attn.bsa_topk = self._bsa_topk
+        self._prewarm()
+
+    def _prewarm(self) -> None:
+        """Pay the engine's one-time costs at enable time, not in the first denoising step (the Metal
+        tier's prewarm, block_sparse_attention_metal.py:298-333).  Only where the model lives on a CUDA
+        device: a model on the host has no engine to warm."""
+        p = next(self.parameters(), None)
+        if p is None or not p.is_cuda:
+            return
+        from .block_sparse_attention_cuda import prewarm_cuda_kernel
+
+        dtype = p.dtype if p.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16
+        with torch.cuda.device(p.device):
+            prewarm_cuda_kernel(head_dim=self.blocks[0].attn.head_dim, dtype=dtype, device=str(p.device))
 
     def disable_bsa(self) -> None:
         """longcat_video_dit.py:259-262."""

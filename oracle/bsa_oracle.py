@@ -331,6 +331,17 @@ def rotate_half(x: np.ndarray) -> np.ndarray:
     return np.stack([-y[..., 1], y[..., 0]], axis=-1).reshape(x.shape)
 
 
+def rms_norm_fp32(x, weight, eps: float, out_dtype: str) -> np.ndarray:
+    """RMSNorm_FP32 (longcat_video/models/blocks.py:55-73): ``(x * rsqrt(mean(x^2) + eps)).astype(dtype)
+    * weight`` with the weight in the input dtype; the norm here in fp64 (the engine's fp32 rsqrt is
+    within a few fp32 ulps of it), each product rounded to fp32 and then to the input dtype."""
+    xf = to_f32(x).astype(np.float64)
+    r = 1.0 / np.sqrt(np.mean(xf * xf, axis=-1, keepdims=True) + eps)
+    n = round_to((xf * r).astype(np.float32), out_dtype)
+    w = round_to(to_f32(weight), out_dtype)
+    return round_to((n * w).astype(np.float32), out_dtype)
+
+
 def apply_rope(x, cos: np.ndarray, sin: np.ndarray, out_dtype: str) -> np.ndarray:
     """rope_3d.py:120-128: fp32 ``x*cos + rotate_half(x)*sin`` (each product and the sum
     rounded to fp32, no fused multiply-add), cast back to the input dtype."""

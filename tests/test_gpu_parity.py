@@ -505,3 +505,204 @@ def test_route_degenerate_rows_fall_back_to_exact(cuda):
     kp[0, 3] = torch.round(kp[0, 3] * 4) / 4
     for k in (1, 30, 150):
         _route_vs_oracle(cuda, qp, kp, k)
+
+
+def test_cond_branch_through_the_engine(cuda):
+    """attention.py:203-223 on the GPU: with conditioning latents the cond frames run BSA on the engine over
+    (num_cond_latents, H, W) and the noise queries attend densely to cond + noise keys.  Each branch is
+    checked against its reference on the same bf16 q/k/v: the cond rows against the oracle's bsa_attention
+    on the RoPE'd q/k, the noise rows against fp32 dense SDPA; the module output is proj(cond | noise)."""
+    from longcat_video.models.attention import Attention
+
+    torch.manual_seed(0)
+    attn = Attention(256, 2).to(cuda).to(torch.bfloat16)
+    attn.enable_bsa = True
+    attn.bsa_sparsity = 0.5  # 4 cond blocks of 4x4x4 -> top-2
+    shape, ncl = (8, 8, 8), 4
+    x = torch.randn((1, 512, 256), device=cuda, dtype=torch.bfloat16)
+    calls = []
+    orig = Attention._process_attn
+
+    def record(self, q, k, v, shape=None, rope_grid=None):
+        out = orig(self, q, k, v, shape=shape, rope_grid=rope_grid)
+        calls.append((q.clone(), k.clone(), v.clone(), shape, out.clone()))
+        return out
+
+    Attention._process_attn = record
+    try:
+        with torch.no_grad():
+            y = attn(x, shape, num_cond_latents=ncl)
+    finally:
+        Attention._process_attn = orig
+    torch.cuda.synchronize()
+    assert len(calls) == 2
+    (qc, kc, vc, cond_shape, oc), (qn, kn, vn, noise_shape, on) = calls
+    assert cond_shape == (ncl, 8, 8) and noise_shape is None and qc.shape[2] == ncl * 64
+    ref_c, _ = orc.bsa_attention(_np(qc), _np(kc), _np(vc), cond_shape, sparsity=0.5, chunk_thw=(4, 4, 4),
+                                 sm_scale=attn.scale)
+    _close(_np(oc), ref_c)
+    ref_n = torch.nn.functional.scaled_dot_product_attention(qn.float(), kn.float(), vn.float(), scale=attn.scale)
+    _close(_np(on), _np(ref_n))
+    want = attn.proj(torch.cat([oc, on], dim=2).transpose(1, 2).reshape(1, 512, 256))
+    assert torch.equal(y, want)
+
+
+def test_kv_cache_continuation_on_gpu(cuda):
+    """attention.py:235-275 on the GPU: the continuation from the cached (k, v) of the conditioning frames
+    gives the noise rows of the one-shot cond + noise forward (bf16, within the output tolerance)."""
+    from longcat_video.models.attention import Attention
+
+    torch.manual_seed(1)
+    attn = Attention(128, 2).to(cuda).to(torch.bfloat16)
+    attn.enable_bsa = True
+    T, Hl, Wl, ncl = 8, 4, 4, 4
+    nc = ncl * Hl * Wl
+    x = torch.randn((1, T * Hl * Wl, 128), device=cuda, dtype=torch.bfloat16)
+    with torch.no_grad():
+        full = attn(x, (T, Hl, Wl), num_cond_latents=ncl)
+        _, kv = attn(x[:, :nc], (ncl, Hl, Wl), return_kv=True)
+        cont = attn.forward_with_kv_cache(x[:, nc:], (T - ncl, Hl, Wl), ncl, kv)
+    _close(_np(cont), _np(full[:, nc:]))
+
+
+def test_hook_writes_the_proj_layout_in_place(cuda):
+    """The BSA path of the hook hands the engine a [B, N, H, D] buffer (viewed as [B, H, N, D]), so proj reads
+    it without the transpose copy of attention.py:228-229; the result is the same as the transpose path."""
+    from longcat_video.models.attention import Attention
+
+    torch.manual_seed(3)
+    attn = Attention(256, 2).to(cuda).to(torch.bfloat16)
+    attn.enable_bsa = True
+    attn.bsa_sparsity = 0.5
+    x = torch.randn((1, 512, 256), device=cuda, dtype=torch.bfloat16)
+    with torch.no_grad():
+        y = attn(x, (8, 8, 8))
+        qkv = attn.qkv(x).reshape(1, 512, 3, 2, 128).permute(2, 0, 3, 1, 4)
+        q, k, v = attn.q_norm(qkv[0]), attn.k_norm(qkv[1]), qkv[2]
+        o = attn._process_attn(q, k, v, shape=(8, 8, 8), rope_grid=(8, 8, 8))
+        want = attn.proj(o.transpose(1, 2).reshape(1, 512, 256))
+    assert torch.equal(y, want)
+
+
+def test_enable_bsa_prewarms_the_engine(cuda):
+    """enable_bsa on a CUDA model runs the engine once (longcat_video_dit.py:220-257 + the Metal tier's
+    prewarm, block_sparse_attention_metal.py:298-333): the library is loaded and no device error is left."""
+    from longcat_video import _native
+    from longcat_video.models.longcat_video_dit import LongCatVideoTransformer3DModel
+
+    dit = LongCatVideoTransformer3DModel(hidden_size=256, depth=2, num_heads=2).to(cuda).to(torch.bfloat16)
+    dit.enable_bsa(backend="cuda")
+    assert _native.library_loaded()
+    assert _native.device_error(clear=True) == 0
+    assert all(b.attn.enable_bsa for b in dit.blocks)
+
+
+def _ulp_distance(a: np.ndarray, b: np.ndarray, dtype: str) -> np.ndarray:
+    """Distance in units in the last place of bf16 / fp16 values (fp32 arrays holding exact 16-bit values)."""
+    if dtype == "bf16":
+        ia = (a.astype(np.float32).view(np.uint32) >> 16).astype(np.int64)
+        ib = (b.astype(np.float32).view(np.uint32) >> 16).astype(np.int64)
+        sign = 0x8000
+    else:
+        ia = a.astype(np.float16).view(np.uint16).astype(np.int64)
+        ib = b.astype(np.float16).view(np.uint16).astype(np.int64)
+        sign = 0x8000
+    oa = np.where(ia & sign, -(ia & (sign - 1)), ia)
+    ob = np.where(ib & sign, -(ib & (sign - 1)), ib)
+    return np.abs(oa - ob)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_qk_norm_rope_pool(cuda, dtype):
+    """RMSNorm_FP32 + 3-D RoPE + pooling in one pass (blocks.py:55-73, rope_3d.py:107-128,
+    block_sparse_attention.py:67-104).  The normalised rows are within one input-dtype ulp of the
+    fp64-normed oracle (the engine's fp32 rsqrt is within a few fp32 ulps); after the rotation, which
+    mixes two such values, within two.  The pooled blocks are bit-exact to the oracle's pooling of the
+    engine's own rows."""
+    from longcat_video import _native
+    from longcat_video.models.rope_3d import RopeTables
+
+    grid = (4, 6, 8)
+    S = 192
+    g = torch.Generator().manual_seed(21)
+    x = (torch.randn((1, 2, S, 128), generator=g) * 3.0).to(dtype).to(cuda)
+    w = (1.0 + 0.1 * torch.randn((128,), generator=g)).to(dtype).to(cuda)
+    dt = "bf16" if dtype == torch.bfloat16 else "fp16"
+    normed = orc.rms_norm_fp32(_np(x), _np(w), 1e-6, dt)
+    pooled_n, x_n = _native.mean_pool(x, (1, 1, S), (1, 1, 64), norm=(w, 1e-6))
+    rt = RopeTables(grid, 128, cuda)
+    pooled, x_rot = _native.mean_pool(x, (1, 1, S), (1, 1, 64), rope=rt.native_args(), norm=(w, 1e-6))
+    torch.cuda.synchronize()
+    d_norm = _ulp_distance(_np(x_n), normed, dt)
+    assert d_norm.max() <= 1 and (d_norm > 0).mean() < 0.01
+    cos, sin = orc.rope_full_tables(grid, 128)
+    assert _ulp_distance(_np(x_rot), orc.apply_rope(normed, cos, sin, dt), dt).max() <= 2
+    # the rotation of the engine's own normalised rows is exact
+    assert _np(x_rot).tobytes() == orc.apply_rope(_np(x_n), cos, sin, dt).tobytes()
+    for pool, rows in ((pooled_n, x_n), (pooled, x_rot)):
+        assert _np(pool).tobytes() == orc.mean_pool_blocks_3d(_np(rows), (1, 1, S), (1, 1, 64)).tobytes()
+
+
+def test_fused_qk_norm_forward_config4(cuda):
+    """Config-4 shape with the raw q/k of the projection: RMSNorm, RoPE and pooling fused.  The routing is
+    exact on the engine's own normalised, rotated q/k; outputs within the contract; and the result agrees
+    with normalising in torch first and fusing only the RoPE."""
+    from longcat_video.models.block_sparse_attention import bsa_attention
+    from longcat_video.models.rope_3d import RopeTables
+    from longcat_video.workloads import CONFIGS, make_qkv
+
+    cfg = CONFIGS["config4"]
+    q, k, v = make_qkv(cfg, cuda, seed=5, heads=2)
+    g = torch.Generator().manual_seed(22)
+    wq, wk = ((1.0 + 0.1 * torch.randn((128,), generator=g)).to(torch.bfloat16).to(cuda) for _ in range(2))
+    rope = RopeTables(cfg.grid, cfg.D, cuda)
+    out, idx = bsa_attention(q, k, v, cfg.shape, chunk_thw=cfg.chunk, topk=cfg.topk, rope=rope,
+                             qk_norm=(wq, wk, 1e-6), return_indices=True)
+    from longcat_video import _native
+
+    _, q_rot = _native.mean_pool(q, cfg.shape, cfg.chunk, rope=rope.native_args(), norm=(wq, 1e-6))
+    _, k_rot = _native.mean_pool(k, cfg.shape, cfg.chunk, rope=rope.native_args(), norm=(wk, 1e-6))
+    torch.cuda.synchronize()
+    qn, kn, vn = _np(q_rot), _np(k_rot), _np(v)
+    qb = orc.mean_pool_blocks_3d(qn, cfg.shape, cfg.chunk)
+    kb = orc.mean_pool_blocks_3d(kn, cfg.shape, cfg.chunk)
+    ref_idx, _ = orc.topk_block_indices(orc.block_routing_scores(qb, kb), topk=cfg.topk)
+    assert np.array_equal(idx.cpu().numpy(), ref_idx)
+    ref = orc.bsa_sparse_attention(qn, kn, vn, ref_idx, cfg.shape, cfg.chunk, qblocks=[0, 700, 1349])
+    _close(orc.to_block_major(_np(out), cfg.shape, cfg.chunk)[:, :, [0, 700, 1349]].reshape(ref.shape), ref)
+
+
+def test_hook_fuses_the_qk_norm(cuda):
+    """The DiT hook on the BSA path passes the raw q/k with the norm weights (no torch RMSNorm); its output
+    is within the contract of the unfused hook (norm in torch, RoPE fused)."""
+    from longcat_video.models.attention import Attention
+
+    torch.manual_seed(4)
+    attn = Attention(256, 2).to(cuda).to(torch.bfloat16)
+    with torch.no_grad():
+        attn.q_norm.weight.mul_(1.1)
+        attn.k_norm.weight.mul_(0.9)
+    attn.enable_bsa = True
+    attn.bsa_sparsity = 0.5
+    x = torch.randn((1, 512, 256), device=cuda, dtype=torch.bfloat16)
+    calls = []
+    orig_norm = type(attn.q_norm).forward
+
+    def counting(self, t):
+        calls.append(1)
+        return orig_norm(self, t)
+
+    type(attn.q_norm).forward = counting
+    try:
+        with torch.no_grad():
+            fused = attn(x, (8, 8, 8))
+            assert not calls  # the norms ran in the engine
+            _, kv = attn(x, (8, 8, 8), return_kv=True)  # the unfused hook (a cache needs the normed k)
+            assert calls
+            qkv = attn.qkv(x).reshape(1, 512, 3, 2, 128).permute(2, 0, 3, 1, 4)
+            o = attn._process_attn(attn.q_norm(qkv[0]), attn.k_norm(qkv[1]), qkv[2], shape=(8, 8, 8),
+                                   rope_grid=(8, 8, 8))
+            unfused = attn.proj(o.transpose(1, 2).reshape(1, 512, 256))
+    finally:
+        type(attn.q_norm).forward = orig_norm
+    _close(_np(fused), _np(unfused))
