@@ -116,7 +116,10 @@ __global__ void __launch_bounds__(kKeyThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
   const int i0 = blockIdx.x * kTile;
-  const int nch = (nb + kTile - 1) / kTile;
+  // this CTA's key-block steps: chunk z of gridDim.z of the row's ceil(nb / 128) steps
+  const int nall = (nb + kTile - 1) / kTile;
+  const int cbeg = static_cast<int>(static_cast<long long>(nall) * blockIdx.z / gridDim.z);
+  const int nch = static_cast<int>(static_cast<long long>(nall) * (blockIdx.z + 1) / gridDim.z) - cbeg;
   if (threadIdx.x == 0) {
     mbar_init(&ks.a_full, 1);
     for (int s = 0; s < 2; ++s) {
@@ -153,8 +156,8 @@ __global__ void __launch_bounds__(kKeyThreads, 1)
         uint8_t* dst = sB + s * 2 * kArrBytes;
         mbar_arrive_expect_tx(&ks.b_full[s], 2 * kArrBytes);
         for (int hh = 0; hh < 2; ++hh) {
-          tma_load_3d(dst + hh * 16384, &m_kh, &ks.b_full[s], 64 * hh, c * kTile, bh);
-          tma_load_3d(dst + kArrBytes + hh * 16384, &m_kl, &ks.b_full[s], 64 * hh, c * kTile, bh);
+          tma_load_3d(dst + hh * 16384, &m_kh, &ks.b_full[s], 64 * hh, (cbeg + c) * kTile, bh);
+          tma_load_3d(dst + kArrBytes + hh * 16384, &m_kl, &ks.b_full[s], 64 * hh, (cbeg + c) * kTile, bh);
         }
       }
       // teardown: every TMA write into shared memory has landed
@@ -217,11 +220,11 @@ __global__ void __launch_bounds__(kKeyThreads, 1)
         tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(s * kTile + 64 * ch + 32 * part),
                   r);
         tmem_ld_wait();
-        const int j0 = c * kTile + 64 * ch + 32 * part;
+        const int j0 = (cbeg + c) * kTile + 64 * ch + 32 * part;
         if (i < nb) {
 #pragma unroll
           for (int e8 = 0; e8 < 4; ++e8) {
-            if (j0 + 8 * e8 < ldk) {  // ldk is a multiple of 8; keys past nb in the row are never read
+            if (j0 + 8 * e8 < ldk) {  // ldk is a multiple of 8; the select clears the keys past nb
               uint4 w;
               w.x = key16(__uint_as_float(r[8 * e8 + 0])) | (key16(__uint_as_float(r[8 * e8 + 1])) << 16);
               w.y = key16(__uint_as_float(r[8 * e8 + 2])) | (key16(__uint_as_float(r[8 * e8 + 3])) << 16);
@@ -245,13 +248,24 @@ __global__ void __launch_bounds__(kKeyThreads, 1)
 
 // ------------------------------------------------------------------ 3. select (one warp per row)
 constexpr int kSelThreads = 256;
+constexpr int kSelWarps = kSelThreads / 32;
+// Per-warp shared state of select_kernel; two key-row buffers of 128 * words bytes follow it (the next
+// row's keys and q row land by cp.async while this row is processed).
 struct SelWarp {
   uint32_t hist[256];
-  float q[kDP];
+  float q[2][kDP];
   uint32_t band_key[kMaxBand];  // exact scores of the band, order-preserving
   int32_t band_id[kMaxBand];
   uint8_t band_sel[kMaxBand];
 };
+constexpr int kSelFixedBytes = (static_cast<int>(sizeof(SelWarp)) + 127) & ~127;
+__host__ __device__ constexpr int sel_warp_bytes(int words) { return kSelFixedBytes + 2 * 128 * words; }
+
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(sdst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
 // fp32 value of an order-preserving bit pattern
 __device__ __forceinline__ float from_ordered(uint32_t o) {
@@ -303,24 +317,23 @@ __device__ __forceinline__ void exact_score2(const float* q, const float* __rest
   s1 = a1;
 }
 
-// One byte of a radix select over the row's 16-bit keys (two per word; `valid` masks the keys past
-// nb): counts the byte `shift` of the keys whose bits above it equal `prefix`, then finds the value
-// of that byte holding the need-th largest key.  Updates prefix (the key bits found so far) and need.
-template <int NP>
-__device__ __forceinline__ void key_radix_byte(const uint32_t (&kw)[NP], int nb, uint32_t* h, int lane, int shift,
+// One byte of a radix select over the row's 16-bit keys (two per word, word e of lane l at kw[32e + l];
+// key 0 marks a slot past nb, as no score maps to 0): counts the byte `shift` of the keys whose bits
+// above it equal `prefix`, then finds the value of that byte holding the need-th largest key.  Updates
+// prefix (the key bits found so far) and need.
+__device__ __forceinline__ void key_radix_byte(const uint32_t* kw, int words, uint32_t* h, int lane, int shift,
                                                uint32_t& prefix, int& need) {
   reinterpret_cast<uint4*>(h)[lane * 2] = make_uint4(0u, 0u, 0u, 0u);
   reinterpret_cast<uint4*>(h)[lane * 2 + 1] = make_uint4(0u, 0u, 0u, 0u);
   __syncwarp();
   const uint32_t hi_mask = shift == 8 ? 0u : 0xff00u;  // bits above the counted byte that must match
-#pragma unroll
-  for (int e = 0; e < NP; ++e) {
-    const uint32_t w = kw[e];
+#pragma unroll 4
+  for (int e = 0; e < words; ++e) {
+    const uint32_t w = kw[32 * e + lane];
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const uint32_t key = half ? (w >> 16) : (w & 0xffffu);
-      if (64 * e + 2 * lane + half < nb && (key & hi_mask) == (prefix & hi_mask))
-        atomicAdd(&h[(key >> shift) & 0xffu], 1u);
+      if (key != 0u && (key & hi_mask) == (prefix & hi_mask)) atomicAdd(&h[(key >> shift) & 0xffu], 1u);
     }
   }
   __syncwarp();
@@ -358,6 +371,67 @@ __device__ __forceinline__ void key_radix_byte(const uint32_t (&kw)[NP], int nb,
   prefix |= static_cast<uint32_t>(digit) << shift;
   need -= static_cast<int>(gt);
   __syncwarp();
+}
+
+// The k-th largest key when it lies within 255 of the row's largest key (the common case: key space is
+// logarithmic, 128 keys per factor of 2, and the top k of a row seldom spans a factor of 4): one
+// histogram of d = max - key over d < 256, where only the keys of that window count, so the bulk of
+// the row (far below) costs a compare and no shared-memory atomic.  Returns false when fewer than k
+// keys lie in the window; T is then unchanged.  Key 0 marks a slot past nb (no score maps to 0).
+__device__ __forceinline__ bool key_window_select(const uint32_t* kw, int words, uint32_t* h, int lane, int k,
+                                                  uint32_t& T) {
+  uint32_t mx = 0;
+#pragma unroll 4
+  for (int e = 0; e < words; ++e) {
+    const uint32_t w = kw[32 * e + lane];
+    mx = max(mx, max(w & 0xffffu, w >> 16));
+  }
+  mx = __reduce_max_sync(0xffffffffu, mx);
+  const uint32_t lim = min(256u, mx);  // d < mx excludes the key-0 slots
+  reinterpret_cast<uint4*>(h)[lane * 2] = make_uint4(0u, 0u, 0u, 0u);
+  reinterpret_cast<uint4*>(h)[lane * 2 + 1] = make_uint4(0u, 0u, 0u, 0u);
+  __syncwarp();
+#pragma unroll 4
+  for (int e = 0; e < words; ++e) {
+    const uint32_t w = kw[32 * e + lane];
+    const uint32_t d0 = mx - (w & 0xffffu), d1 = mx - (w >> 16);
+    if (d0 < lim) atomicAdd(&h[d0], 1u);
+    if (d1 < lim) atomicAdd(&h[d1], 1u);
+  }
+  __syncwarp();
+  // bins 8l .. 8l+7 on lane l, in order of decreasing key; inclusive prefix over the lanes
+  const uint4 c0 = reinterpret_cast<const uint4*>(h)[lane * 2];
+  const uint4 c1 = reinterpret_cast<const uint4*>(h)[lane * 2 + 1];
+  const uint32_t cnt[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+  uint32_t tot = 0;
+#pragma unroll
+  for (int b = 0; b < 8; ++b) tot += cnt[b];
+  uint32_t pre = tot;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t o = __shfl_up_sync(0xffffffffu, pre, off);
+    if (lane >= off) pre += o;
+  }
+  const uint32_t kk = static_cast<uint32_t>(k);
+  const bool mine = pre - tot < kk && kk <= pre;
+  uint32_t dk = 0;
+  if (mine) {
+    uint32_t run = pre - tot;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      run += cnt[b];
+      if (run >= kk) {
+        dk = 8u * static_cast<uint32_t>(lane) + static_cast<uint32_t>(b);
+        break;
+      }
+    }
+  }
+  const uint32_t bal = __ballot_sync(0xffffffffu, mine);
+  __syncwarp();
+  if (!bal) return false;
+  dk = __shfl_sync(0xffffffffu, dk, __ffs(bal) - 1);
+  T = mx - dk;
+  return true;
 }
 
 // Smallest key whose interval minus e lies above U (keys at or above it are sure), and largest finite
@@ -401,50 +475,81 @@ __device__ __forceinline__ void band_keys(uint32_t T, float L, float U, float e,
   }
 }
 
-// NP words of two keys per lane: lane l holds keys 64e + 2l and 64e + 2l + 1 in word e (nb <= 64 NP).
-template <int NP>
-__global__ void __launch_bounds__(kSelThreads, 2)
+// A key the bound does not decide: below the sure keys and above the out keys, or non-finite (1 .. 0x7f:
+// NaN, -inf); key 0 is an empty slot.
+__device__ __forceinline__ bool in_band(uint32_t key, uint32_t ks, uint32_t ko) {
+  return key < ks && (key > ko || key - 1u < 0x7fu);
+}
+
+// One warp per row; the row's keys sit in shared memory as `words` 32-bit words per lane (lane l holds
+// keys 64e + 2l and 64e + 2l + 1 in word e).  Dynamic shared memory: kSelWarps * sel_warp_bytes(words).
+__global__ void __launch_bounds__(kSelThreads, 3)
     select_kernel(const uint16_t* __restrict__ keys, int ldk, const float* __restrict__ qp,
                   const float* __restrict__ kp, const float* __restrict__ nrm, const float* __restrict__ nkmax, int rows,
                   int nb, int D, int k, int32_t* idx, int* fb_count, int* fb_rows) {
-  __shared__ SelWarp sw_all[kSelThreads / 32];
+  extern __shared__ __align__(128) uint8_t sel_smem[];
   const int lane = threadIdx.x & 31;
-  SelWarp& sw = sw_all[threadIdx.x >> 5];
+  const int words = (nb + 63) >> 6;
+  uint8_t* wbase = sel_smem + static_cast<size_t>(threadIdx.x >> 5) * sel_warp_bytes(words);
+  SelWarp& sw = *reinterpret_cast<SelWarp*>(wbase);
+  uint32_t* kbuf = reinterpret_cast<uint32_t*>(wbase + kSelFixedBytes);  // [2][32 * words]
   const uint32_t lt = (1u << lane) - 1u;
-  const int nw = gridDim.x * (kSelThreads / 32);
-  for (int row = blockIdx.x * (kSelThreads / 32) + (threadIdx.x >> 5); row < rows; row += nw) {
+  const int nw = gridDim.x * kSelWarps;
+  int row = blockIdx.x * kSelWarps + (threadIdx.x >> 5);
+  if (k == nb) {  // every block: the ids in order
+    for (; row < rows; row += nw)
+      for (int j = lane; j < nb; j += 32) idx[static_cast<long long>(row) * k + j] = j;
+    return;
+  }
+  // slots from nb up to 64 * words hold key 0 (no score maps to 0): the ones no copy reaches are set
+  // once here, the padding slots nb .. ldk-1 that a copy brings are cleared after each row lands
+  for (int b = 0; b < 2; ++b) {
+    uint16_t* kb = reinterpret_cast<uint16_t*>(kbuf + b * 32 * words);
+    for (int j = ldk + lane; j < 64 * words; j += 32) kb[j] = 0;
+  }
+  const int kchunks = ldk >> 3, qchunks = D >> 2;  // 16-byte pieces of a key row and of a q row
+  auto fetch = [&](int r, int b) {
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(keys + static_cast<long long>(r) * ldk);
+    uint8_t* dst = reinterpret_cast<uint8_t*>(kbuf + b * 32 * words);
+    for (int c = lane; c < kchunks; c += 32) cp_async16(dst + 16 * c, src + 16 * c);
+    const float* qs = qp + static_cast<long long>(r) * D;
+    for (int c = lane; c < qchunks; c += 32) cp_async16(sw.q[b] + 4 * c, qs + 4 * c);
+  };
+  if (row < rows) fetch(row, 0);
+  cp_async_commit();
+  for (int b = 0; row < rows; row += nw, b ^= 1) {
+    if (row + nw < rows) fetch(row + nw, b ^ 1);
+    cp_async_commit();
+    cp_async_wait_prev();  // this row's group has landed (the next row's may still be in flight)
+    __syncwarp();
+    const uint32_t* kw = kbuf + b * 32 * words;
+    if (lane < ldk - nb) reinterpret_cast<uint16_t*>(kbuf + b * 32 * words)[nb + lane] = 0;
+    __syncwarp();
+    const float* q = sw.q[b];
     const int bh = row / nb;
     int32_t* out = idx + static_cast<long long>(row) * k;
-    if (k == nb) {  // every block: the ids in order
-      for (int j = lane; j < nb; j += 32) out[j] = j;
-      continue;
-    }
-    __syncwarp();
-    for (int d = lane; d < D; d += 32) sw.q[d] = __ldg(qp + static_cast<long long>(row) * D + d);
-    const uint32_t* krow = reinterpret_cast<const uint32_t*>(keys + static_cast<long long>(row) * ldk);
-    uint32_t kw[NP];  // word e: keys 64e + 2l (low half) and 64e + 2l + 1 (high half); validity is j < nb
-#pragma unroll
-    for (int e = 0; e < NP; ++e) kw[e] = 64 * e + 2 * lane < nb ? __ldg(krow + 32 * e + lane) : 0u;
     const float ebound = __fmul_ru(__fmul_ru(kErrC, __ldg(nrm + row)), __ldg(nkmax + bh));
-    // the k-th largest key T: high byte, then low byte
+    // the k-th largest key T: a window below the row's largest key, else a radix select (high byte,
+    // then low byte)
     uint32_t T = 0;
-    int need = k;
-    key_radix_byte<NP>(kw, nb, sw.hist, lane, 8, T, need);
-    key_radix_byte<NP>(kw, nb, sw.hist, lane, 0, T, need);
+    if (!key_window_select(kw, words, sw.hist, lane, k, T)) {
+      int need = k;
+      key_radix_byte(kw, words, sw.hist, lane, 8, T, need);
+      key_radix_byte(kw, words, sw.hist, lane, 0, T, need);
+    }
     // s_(k) in [L, U]
     const float L = __fsub_rd(key_low(T), ebound);
     const float U = __fadd_ru(key_high(T), ebound);
     uint32_t ks = 0xff81u, ko = 0x7fu;
     if (ebound < INFINITY) band_keys(T, L, U, ebound, lane, ks, ko);
-    // classes: sure (key >= ks), out (0x80 <= key <= ko), band (the other valid keys); band ids ascending
+    // classes: sure (key >= ks), out (0x80 <= key <= ko), band (the other keys but 0); band ids ascending
     int n_sure = 0, pos = 0;
-#pragma unroll
-    for (int e = 0; e < NP; ++e) {
-      const uint32_t k0 = kw[e] & 0xffffu, k1 = kw[e] >> 16;
-      const bool v0 = 64 * e + 2 * lane < nb, v1 = 64 * e + 2 * lane + 1 < nb;
-      n_sure += (v0 && k0 >= ks) + (v1 && k1 >= ks);
-      const bool b0 = v0 && k0 < ks && (k0 > ko || k0 < 0x80u);
-      const bool b1 = v1 && k1 < ks && (k1 > ko || k1 < 0x80u);
+#pragma unroll 2
+    for (int e = 0; e < words; ++e) {
+      const uint32_t w = kw[32 * e + lane];
+      const uint32_t k0 = w & 0xffffu, k1 = w >> 16;
+      n_sure += (k0 >= ks) + (k1 >= ks);
+      const bool b0 = in_band(k0, ks, ko), b1 = in_band(k1, ks, ko);
       const uint32_t m0 = __ballot_sync(0xffffffffu, b0), m1 = __ballot_sync(0xffffffffu, b1);
       const int p0 = pos + __popc(m0 & lt) + __popc(m1 & lt);
       if (b0 && p0 < kMaxBand) sw.band_id[p0] = 64 * e + 2 * lane;
@@ -456,6 +561,7 @@ __global__ void __launch_bounds__(kSelThreads, 2)
     const bool fast = ebound < INFINITY && n_band <= kMaxBand && n_sure <= k && n_sure + n_band >= k;
     if (!fast) {  // scored exactly in full by fallback_kernel
       if (lane == 0) fb_rows[atomicAdd(fb_count, 1)] = row;
+      __syncwarp();
       continue;
     }
     __syncwarp();
@@ -464,7 +570,7 @@ __global__ void __launch_bounds__(kSelThreads, 2)
     if (lane < n_band) {
       float s0, s1;
       const float* r1 = lane + 32 < n_band ? kbase + static_cast<long long>(sw.band_id[lane + 32]) * D : nullptr;
-      exact_score2(sw.q, kbase + static_cast<long long>(sw.band_id[lane]) * D, r1, D, s0, s1);
+      exact_score2(q, kbase + static_cast<long long>(sw.band_id[lane]) * D, r1, D, s0, s1);
       sw.band_key[lane] = topk::ordered_key(s0);
       if (r1) sw.band_key[lane + 32] = topk::ordered_key(s1);
     }
@@ -473,31 +579,29 @@ __global__ void __launch_bounds__(kSelThreads, 2)
     const int rest = k - n_sure;
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
-      const int b = lane + 32 * t;
-      if (b < n_band) {
-        const uint32_t mk = sw.band_key[b];
+      const int b2 = lane + 32 * t;
+      if (b2 < n_band) {
+        const uint32_t mk = sw.band_key[b2];
         int rank = 0;
         for (int u = 0; u < n_band; ++u) {
           const uint32_t o = sw.band_key[u];
-          rank += (o > mk || (o == mk && u < b)) ? 1 : 0;
+          rank += (o > mk || (o == mk && u < b2)) ? 1 : 0;
         }
-        sw.band_sel[b] = rank < rest;
+        sw.band_sel[b2] = rank < rest;
       }
     }
     __syncwarp();
     // ascending emission: sure blocks and the chosen band blocks
     int taken = 0, bpos = 0;
-#pragma unroll
-    for (int e = 0; e < NP; ++e) {
-      if (64 * e >= nb) break;  // warp-uniform
-      const uint32_t k0 = kw[e] & 0xffffu, k1 = kw[e] >> 16;
-      const bool v0 = 64 * e + 2 * lane < nb, v1 = 64 * e + 2 * lane + 1 < nb;
-      const bool b0 = v0 && k0 < ks && (k0 > ko || k0 < 0x80u);
-      const bool b1 = v1 && k1 < ks && (k1 > ko || k1 < 0x80u);
+#pragma unroll 2
+    for (int e = 0; e < words; ++e) {
+      const uint32_t w = kw[32 * e + lane];
+      const uint32_t k0 = w & 0xffffu, k1 = w >> 16;
+      const bool b0 = in_band(k0, ks, ko), b1 = in_band(k1, ks, ko);
       const uint32_t m0 = __ballot_sync(0xffffffffu, b0), m1 = __ballot_sync(0xffffffffu, b1);
       const int p0 = bpos + __popc(m0 & lt) + __popc(m1 & lt);
-      const bool s0 = (v0 && k0 >= ks) || (b0 && sw.band_sel[p0]);
-      const bool s1 = (v1 && k1 >= ks) || (b1 && sw.band_sel[p0 + b0]);
+      const bool s0 = k0 >= ks || (b0 && sw.band_sel[p0]);
+      const bool s1 = k1 >= ks || (b1 && sw.band_sel[p0 + b0]);
       const uint32_t t0 = __ballot_sync(0xffffffffu, s0), t1 = __ballot_sync(0xffffffffu, s1);
       const int q0 = taken + __popc(t0 & lt) + __popc(t1 & lt);
       if (s0) out[q0] = 64 * e + 2 * lane;
@@ -506,7 +610,9 @@ __global__ void __launch_bounds__(kSelThreads, 2)
       bpos += __popc(m0) + __popc(m1);
     }
     if (lane == 0 && taken != k) atomicCAS(&g_route_err, 0, 410);
+    __syncwarp();
   }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
 }
 
 // Rows the fast path could not bound: every score exact (one warp per row), then the register radix
@@ -599,25 +705,64 @@ int launch_route(const RouteArgs& a, cudaStream_t stream) {
         if (dev < 64) configured[dev] = true;
       }
     }
-    const dim3 grid((a.nb + kTile - 1) / kTile, a.BH, 1);
+    // key-block steps split over gridDim.z CTAs when the (query tile, head) grid alone would leave SMs
+    // idle or a large last wave: the split minimising waves x (steps + one A load) per CTA
+    const int gx = (a.nb + kTile - 1) / kTile;
+    int split = 1;
+    long long best = -1;
+    for (int z = 1; z <= gx && z <= 16; ++z) {
+      const long long ctas = static_cast<long long>(gx) * a.BH * z;
+      const long long cost = ((ctas + sms - 1) / sms) * ((gx + z - 1) / z + 1);
+      if (best < 0 || cost < best) {
+        best = cost;
+        split = z;
+      }
+    }
+    const dim3 grid(gx, a.BH, split);
     if (grid.y > 65535u) return BSA_ERR_SHAPE;
     key_kernel<<<grid, kKeyThreads, kKeySmemBytes, stream>>>(maps[0], maps[1], maps[2], maps[3], a.nb,
                                                              static_cast<int>(ldk), keys);
   }
-  // 3. select, then the exact full-row path for the rows the band could not settle
+  // 3. select (grid: as many CTAs as fit on the SMs), then the exact full-row path for the rows the
+  //    band could not settle
   {
-    long long grid = (static_cast<long long>(rows) + 7) / 8;
-    if (grid > static_cast<long long>(sms) * 12) grid = static_cast<long long>(sms) * 12;
-    const unsigned fgrid = static_cast<unsigned>(sms) * 2;
-    if (a.nb <= 64 * 24) {
-      select_kernel<24><<<static_cast<unsigned>(grid), kSelThreads, 0, stream>>>(
-          keys, static_cast<int>(ldk), a.qp, a.kp, nrm, nkmax, rows, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
-      fallback_kernel<48><<<fgrid, kSelThreads, 0, stream>>>(a.qp, a.kp, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
-    } else {
-      select_kernel<48><<<static_cast<unsigned>(grid), kSelThreads, 0, stream>>>(
-          keys, static_cast<int>(ldk), a.qp, a.kp, nrm, nkmax, rows, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
-      fallback_kernel<96><<<fgrid, kSelThreads, 0, stream>>>(a.qp, a.kp, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
+    const int words = (a.nb + 63) / 64;
+    const int sel_smem = kSelWarps * sel_warp_bytes(words);
+    // the attribute only grows (a concurrent launch with a larger row never sees it lowered); the
+    // occupancy of the last row length is kept per device
+    static std::mutex mu;
+    static int attr_bytes[64] = {}, occ_bytes[64] = {}, occ_ctas[64] = {};
+    int per_sm = 0;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      const bool cached = dev < 64 && occ_bytes[dev] == sel_smem;
+      if (dev >= 64 || attr_bytes[dev] < sel_smem) {
+        if (cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sel_smem) != cudaSuccess)
+          return BSA_ERR_CUDA;
+        if (dev < 64) attr_bytes[dev] = sel_smem;
+      }
+      if (cached) {
+        per_sm = occ_ctas[dev];
+      } else {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, select_kernel, kSelThreads, sel_smem) !=
+                cudaSuccess ||
+            per_sm < 1)
+          return BSA_ERR_CUDA;
+        if (dev < 64) {
+          occ_bytes[dev] = sel_smem;
+          occ_ctas[dev] = per_sm;
+        }
+      }
     }
+    long long grid = (static_cast<long long>(rows) + kSelWarps - 1) / kSelWarps;
+    if (grid > static_cast<long long>(sms) * per_sm) grid = static_cast<long long>(sms) * per_sm;
+    select_kernel<<<static_cast<unsigned>(grid), kSelThreads, sel_smem, stream>>>(
+        keys, static_cast<int>(ldk), a.qp, a.kp, nrm, nkmax, rows, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
+    const unsigned fgrid = static_cast<unsigned>(sms) * 2;
+    if (a.nb <= 64 * 24)
+      fallback_kernel<48><<<fgrid, kSelThreads, 0, stream>>>(a.qp, a.kp, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
+    else
+      fallback_kernel<96><<<fgrid, kSelThreads, 0, stream>>>(a.qp, a.kp, a.nb, a.D, a.topk, a.idx, fb_count, fb_rows);
   }
   return cudaGetLastError() == cudaSuccess ? BSA_OK : BSA_ERR_CUDA;
 }

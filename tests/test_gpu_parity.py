@@ -507,6 +507,19 @@ def test_route_degenerate_rows_fall_back_to_exact(cuda):
         _route_vs_oracle(cuda, qp, kp, k)
 
 
+def test_route_wide_rows_take_the_radix_select(cuda):
+    """Rows whose k-th largest score lies far (more than a factor of 4) below the row's largest: the window
+    next to the largest key cannot hold the k-th key and the select falls back to the two-byte radix.  A
+    few key blocks scaled by 1000 in head 0, and k near the median score (mixed signs) in both heads."""
+    g = torch.Generator().manual_seed(13)
+    nb, D = 1350, 128
+    qp = torch.randn((1, 2, nb, D), generator=g)
+    kp = torch.randn((1, 2, nb, D), generator=g)
+    kp[0, 0, ::100] *= 1000.0
+    for k in (10, 85, 675):
+        _route_vs_oracle(cuda, qp, kp, k)
+
+
 def test_cond_branch_through_the_engine(cuda):
     """attention.py:203-223 on the GPU: with conditioning latents the cond frames run BSA on the engine over
     (num_cond_latents, H, W) and the noise queries attend densely to cond + noise keys.  Each branch is
