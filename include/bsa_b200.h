@@ -197,6 +197,17 @@ int bsa_ipc_open(const unsigned char* handle, void** ptr);
 int bsa_ipc_close(void* ptr);
 int bsa_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
                 void* stream);
+/* bsa_copy_3d  : `depth` slices of `height` rows of `width` bytes; row pitches dpitch / spitch and slice
+ *                pitches dslice / sslice in bytes (a slice pitch is a multiple of its row pitch and holds
+ *                `height` rows).  The copy engine pays a fixed cost per call (about 11 us measured on
+ *                B200 over NVLink, against 4 us for moving 2.6 MiB), so one call should move as much as
+ *                the layouts allow: the exchange moves q, k and v of a head group from a peer in one call.
+ * bsa_copy_3d_list: n bsa_copy_3d calls in order on one stream, from desc[9*i .. 9*i+8] = (dst, dpitch,
+ *                dslice, src, spitch, sslice, width, height, depth) -- one host call for an exchange's whole
+ *                copy plan of a head group. */
+int bsa_copy_3d(void* dst, int64_t dpitch, int64_t dslice, const void* src, int64_t spitch, int64_t sslice,
+                int64_t width, int64_t height, int64_t depth, void* stream);
+int bsa_copy_3d_list(const int64_t* desc, int n, void* stream);
 
 #ifdef __cplusplus
 }

@@ -72,4 +72,35 @@ int bsa_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int6
   return BSA_OK;
 }
 
+int bsa_copy_3d(void* dst, int64_t dpitch, int64_t dslice, const void* src, int64_t spitch, int64_t sslice,
+                int64_t width, int64_t height, int64_t depth, void* stream) {
+  if (depth == 1) return bsa_copy_2d(dst, dpitch, src, spitch, width, height, stream);
+  if (!dst || !src) return bsa::set_error(BSA_ERR_ARG, "bsa_copy_3d: null pointer");
+  if (width < 0 || height < 0 || depth < 0 || dpitch < width || spitch < width || dpitch <= 0 || spitch <= 0 ||
+      dslice % dpitch || sslice % spitch || dslice < dpitch * height || sslice < spitch * height)
+    return bsa::set_error(BSA_ERR_ARG, "bsa_copy_3d: bad extents");
+  if (width == 0 || height == 0 || depth == 0) return BSA_OK;
+  cudaMemcpy3DParms prm = {};
+  prm.srcPtr = make_cudaPitchedPtr(const_cast<void*>(src), static_cast<size_t>(spitch), static_cast<size_t>(width),
+                                   static_cast<size_t>(sslice / spitch));
+  prm.dstPtr = make_cudaPitchedPtr(dst, static_cast<size_t>(dpitch), static_cast<size_t>(width),
+                                   static_cast<size_t>(dslice / dpitch));
+  prm.extent = make_cudaExtent(static_cast<size_t>(width), static_cast<size_t>(height), static_cast<size_t>(depth));
+  prm.kind = cudaMemcpyDefault;
+  if (cudaMemcpy3DAsync(&prm, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return bsa::set_error(BSA_ERR_CUDA, "bsa_copy_3d: %s", cudaGetErrorString(cudaGetLastError()));
+  return BSA_OK;
+}
+
+int bsa_copy_3d_list(const int64_t* desc, int n, void* stream) {
+  if (n < 0 || (n > 0 && !desc)) return bsa::set_error(BSA_ERR_ARG, "bsa_copy_3d_list: bad argument");
+  for (int i = 0; i < n; ++i) {
+    const int64_t* d = desc + 9 * static_cast<int64_t>(i);
+    const int rc = bsa_copy_3d(reinterpret_cast<void*>(d[0]), d[1], d[2], reinterpret_cast<const void*>(d[3]), d[4],
+                               d[5], d[6], d[7], d[8], stream);
+    if (rc) return rc;
+  }
+  return BSA_OK;
+}
+
 }  // extern "C"

@@ -58,6 +58,9 @@ _SIGNATURES = {
     "bsa_ipc_open": ([ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)], _i),
     "bsa_ipc_close": ([_vp], _i),
     "bsa_copy_2d": ([_vp, ctypes.c_int64, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp], _i),
+    "bsa_copy_3d": ([_vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                     ctypes.c_int64, ctypes.c_int64, _vp], _i),
+    "bsa_copy_3d_list": ([_vp, _i, _vp], _i),
     "bsa_attention_indices_ex": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i,
                                   _i, _i, _i, _f, _vp, _c_i64p, _i, _vp], _i),
     "bsa_forward_ex": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i, _i, _i, _i, _f,
@@ -446,6 +449,14 @@ def ipc_close(ptr: int) -> None:
 def copy_2d(dst: int, dpitch: int, src: int, spitch: int, width: int, height: int, stream) -> None:
     """`height` rows of `width` bytes between any local / mapped-peer addresses, on `stream`."""
     _check(lib().bsa_copy_2d(dst, dpitch, src, spitch, width, height, stream.cuda_stream), "bsa_copy_2d")
+
+
+def copy_3d_list(desc, n: int, stream) -> None:
+    """n copies of a prebuilt ctypes int64 array of (dst, dpitch, dslice, src, spitch, sslice, width, height,
+    depth) rows (bsa_copy_3d), in order on `stream`, in one host call."""
+    if n:
+        _check(lib().bsa_copy_3d_list(ctypes.cast(desc, ctypes.c_void_p), int(n), stream.cuda_stream),
+               "bsa_copy_3d_list")
 
 
 class _DevBuf:

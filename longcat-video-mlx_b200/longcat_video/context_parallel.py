@@ -7,13 +7,17 @@ second all-to-all returns the output to sequence shards.  The upstream PyTorch m
 with ``ulysses_wrapper`` / ``context_parallel_util``, which the MLX port dropped
 (rope_3d.py:14; stubbed in tests/parity/test_dit_block_parity.py:88-112).
 
-Plumbing is ``torch.distributed.all_to_all_single`` (NCCL over NVLink on GPUs, gloo on CPU for
-tests).  Q, K and V travel in one collective.  Pre-RoPE Q/K travel and RoPE is applied after the
-exchange, because the rotation needs each token's global position.
+Two exchanges move the pieces (``ulysses_bsa_attention``): on CUDA tensors of an NCCL group the
+default is ``PeerExchange`` -- persistent CUDA-IPC buffers and copies on the copy engines over NVLink,
+ordered by three 4-byte NCCL all-reduces per call -- and otherwise point-to-point messages of the
+process group (NCCL, or gloo on CPU for tests).  ``seq_to_heads`` / ``heads_to_seq`` are the plain
+``all_to_all_single`` forms.  Pre-RoPE Q/K travel and RoPE is applied after the exchange, because the
+rotation needs each token's global position.
 """
 
 from __future__ import annotations
 
+import math
 from typing import Optional, Tuple
 
 import torch
@@ -135,13 +139,15 @@ class PeerExchange:
     and local ones: two whole-sequence input slots [3, B, Hl, S, D] and two output slots
     [B, Hl, S, D] (Hl = heads of one group owned by this rank).
 
-    One call: stage q/k/v (local copy), barrier, then per head group g a copy-in stream pulls the
-    group's pieces from every peer's stage into slot g%2 (one 2-D copy per peer, tensor and batch),
-    the compute stream runs BSA on it, and a copy-out stream pushes each peer's token range of the
-    output straight into that peer's out_recv.  A final barrier (after this rank's last push)
-    means every peer's pushes into this rank's out_recv are complete.  Copy engines carry every
-    transfer over NVLink, so the attention kernel keeps all SMs.  Two barriers per call (a 4-byte
-    all-reduce each); no host synchronisation.
+    One call: stage group 0's heads of q/k/v (local copy), barrier, stage the other groups, barrier;
+    per head group g a copy-in stream pulls the group's q/k/v pieces from every peer's stage into slot
+    g%2 (one 3-D copy per peer and batch; group 0 right after the first barrier, the others after the
+    second), the compute stream runs BSA on it, and a copy-out stream pushes each peer's token range of
+    the output straight into that peer's out_recv.  A final barrier (after this rank's last push) means
+    every peer's pushes into this rank's out_recv are complete.  Copy engines carry every transfer
+    over NVLink, so the attention kernel keeps all SMs.  Three barriers per call (two with one head
+    group; a 4-byte all-reduce each); no host synchronisation.  The copy plan of every group is built
+    once (``_plan``) and issued with one host call per stream.
     """
 
     def __init__(self, B: int, H: int, Sl: int, D: int, dtype: torch.dtype, groups: int, group, device):
@@ -185,80 +191,118 @@ class PeerExchange:
         self.s_comp = [torch.cuda.Stream(device) for _ in range(COMPUTE_STREAMS)]
         self.s_join = [torch.cuda.Stream(device) for _ in range(2)]
         self._native = _native
+        self._plan()
+        # events reused by every call (recording again replaces the previous record; waits already
+        # queued keep the record they saw)
+        G = self.G
+        self.ev_start = torch.cuda.Event()
+        self.ev_staged = torch.cuda.Event()
+        self.ev_in = [[torch.cuda.Event() for _ in self.s_in] for _ in range(G)]
+        self.ev_comp = [torch.cuda.Event() for _ in range(G)]
+        self.ev_out = [[torch.cuda.Event() for _ in self.s_out] for _ in range(G)]
+        self.ev_push = [torch.cuda.Event() for _ in range(G)]
+        self._slot_bufs = {}
+
+    def _plan(self):
+        """Every copy of a call, fixed once: the buffers are persistent, so each head group's pulls (peers'
+        stages -> input slot g % 2) and pushes (output slot g % 2 -> peers' out_recv) are lists of copies,
+        one list per copy stream, issued by one host call each (bsa_copy_3d_list).  The copy engine pays a
+        fixed cost per call, so a pull moves q, k and v of the group's heads from one peer in one 3-D copy
+        (slices: the tensors; rows: the heads; a row: the peer's token range of one head)."""
+        import ctypes
+
+        P, r, B, H, Sl, D, S, Hl, Hg, e = (self.P, self.rank, self.B, self.H, self.Sl, self.D, self.S, self.Hl,
+                                            self.Hg, self.elt)
+        piece, row = Sl * D * e, S * D * e
+        nin, nout = len(self.s_in), len(self.s_out)
+        self.pull, self.push = [], []
+
+        def pack(rows):
+            arr = (ctypes.c_int64 * (9 * max(1, len(rows))))(*[x for rw in rows for x in rw])
+            return arr, len(rows)
+
+        for g in range(self.G):
+            sl = g % 2
+            h0 = g * Hg + r * Hl  # first head of this group that this rank computes
+            ins = [[] for _ in range(nin)]
+            dst0 = self.recv_in[sl].data_ptr()
+            for p in range(P):
+                for b in range(B):
+                    src = self.peer_stage[p] + (b * H + h0) * piece       # stage [3, B, H, Sl, D]
+                    dst = dst0 + (b * Hl * S + p * Sl) * D * e            # recv_in [3, B, Hl, S, D]
+                    ins[(p + r) % nin].append((dst, row, B * Hl * row, src, piece, B * H * piece, piece, Hl, 3))
+            outs = [[] for _ in range(nout)]
+            src0 = self.o_slot[sl].data_ptr()
+            for p in range(P):
+                for b in range(B):
+                    src = src0 + (b * Hl * S + p * Sl) * D * e            # o_slot [B, Hl, S, D]
+                    dst = self.peer_outr[p] + (b * H + h0) * piece        # out_recv [B, H, Sl, D]
+                    outs[(p + r) % nout].append((dst, piece, piece * Hl, src, row, row * Hl, piece, Hl, 1))
+            self.pull.append([pack(x) for x in ins])
+            self.push.append([pack(x) for x in outs])
+
+    def slot_buffers(self, sl: int, nb: int, topk: int, scratch_bytes: int):
+        """Per-slot routing output and scratch of the compute step (allocated once per size)."""
+        key = (sl, nb, topk, scratch_bytes)
+        bufs = self._slot_bufs.get(key)
+        if bufs is None:
+            idx = torch.empty((self.B, self.Hl, nb, topk), device=self.device, dtype=torch.int32)
+            scratch = torch.empty((max(16, scratch_bytes),), device=self.device, dtype=torch.uint8)
+            bufs = self._slot_bufs[key] = (idx, scratch)
+        return bufs
 
     def _barrier(self):
         dist.all_reduce(self.flag, group=self.group)  # on the current stream; no host wait
 
     def run(self, q, k, v, compute) -> torch.Tensor:
-        """q, k, v: [B, H, S/P, D] shards; compute(qh, kh, vh, out) runs BSA on one group's
+        """q, k, v: [B, H, S/P, D] shards; compute(qh, kh, vh, out, slot) runs BSA on one group's
         whole-sequence heads [B, Hl, S, D] into out.  Returns the output shard [B, H, S/P, D]."""
-        nat, P, r = self._native, self.P, self.rank
-        B, H, Sl, D, S, Hl, Hg, e = self.B, self.H, self.Sl, self.D, self.S, self.Hl, self.Hg, self.elt
+        nat = self._native
         C = torch.cuda.current_stream(self.device)
+        # stage group 0's heads first: its pulls start while the other groups stage
+        hg = self.Hg
         for t, x in enumerate((q, k, v)):
-            self.stage[t].copy_(x)
-        self._barrier()  # every rank has staged this call's inputs and finished its previous call
-        ev_start = torch.cuda.Event()
-        ev_start.record(C)
+            self.stage[t][:, :hg].copy_(x[:, :hg])
+        self._barrier()  # every rank has staged group 0 and finished its previous call
+        self.ev_start.record(C)
         for st in self.s_in + self.s_out + self.s_comp:
-            st.wait_event(ev_start)
-        ev_comp, ev_push = [], []
-        piece, row = Sl * D * e, S * D * e
-        nx = len(self.s_in)
+            st.wait_event(self.ev_start)
+        if self.G > 1:
+            for t, x in enumerate((q, k, v)):
+                self.stage[t][:, hg:].copy_(x[:, hg:])
+            self._barrier()  # every rank has staged every group
+            self.ev_staged.record(C)
         for g in range(self.G):
             sl = g % 2
-            h0 = g * Hg + r * Hl  # first head of this group that this rank computes
-            # copy-in: one stream per peer (mod the stream count) so several copy engines share the pull
-            ev_in = []
+            # copy-in: this group's pieces from every peer, one host call per copy stream
             for i, st in enumerate(self.s_in):
+                if g == 1:
+                    st.wait_event(self.ev_staged)
                 if g >= 2:
-                    st.wait_event(ev_comp[g - 2])  # input slot free
-            dst0 = self.recv_in[sl].data_ptr()
-            for p in range(P):
-                st = self.s_in[(p + r) % nx]
-                for t in range(3):
-                    for b in range(B):
-                        src = self.peer_stage[p] + ((t * B + b) * H + h0) * piece
-                        dst = dst0 + ((t * B + b) * Hl * S + p * Sl) * D * e
-                        nat.copy_2d(dst, row, src, piece, piece, Hl, st)
-            for st in self.s_in:
-                ev = torch.cuda.Event()
-                ev.record(st)
-                ev_in.append(ev)
+                    st.wait_event(self.ev_comp[g - 2])  # input slot free
+                arr, n = self.pull[g][i]
+                nat.copy_3d_list(arr, n, st)
+                self.ev_in[g][i].record(st)
             # compute (with COMPUTE_STREAMS > 1 groups alternate between streams, so one group's
             # kernels can start on SMs that the previous group's attention tail leaves idle)
             cs = self.s_comp[g % len(self.s_comp)]
-            for ev in ev_in:
+            for ev in self.ev_in[g]:
                 cs.wait_event(ev)
             if g >= 2:
-                cs.wait_event(ev_push[g - 2])  # output slot free
+                cs.wait_event(self.ev_push[g - 2])  # output slot free
             xin, o = self.recv_in[sl], self.o_slot[sl]
             with torch.cuda.stream(cs):
-                compute(xin[0], xin[1], xin[2], o)
-            ec = torch.cuda.Event()
-            ec.record(cs)
-            ev_comp.append(ec)
-            src0 = o.data_ptr()
-            ev_out = []
-            for st in self.s_out:
-                st.wait_event(ec)
-            for p in range(P):
-                st = self.s_out[(p + r) % len(self.s_out)]
-                for b in range(B):
-                    src = src0 + (b * Hl * S + p * Sl) * D * e
-                    dst = self.peer_outr[p] + (b * H + h0) * piece
-                    nat.copy_2d(dst, piece, src, row, piece, Hl, st)
-            for st in self.s_out:
-                ev = torch.cuda.Event()
-                ev.record(st)
-                ev_out.append(ev)
-            # one event that covers every copy-out stream of this group
+                compute(xin[0], xin[1], xin[2], o, sl)
+            self.ev_comp[g].record(cs)
+            # copy-out: each peer's token range of the output straight into its out_recv
             joint = self.s_join[g % 2]
-            for ev in ev_out:
-                joint.wait_event(ev)
-            ep = torch.cuda.Event()
-            ep.record(joint)
-            ev_push.append(ep)
+            for i, st in enumerate(self.s_out):
+                st.wait_event(self.ev_comp[g])
+                arr, n = self.push[g][i]
+                nat.copy_3d_list(arr, n, st)
+                self.ev_out[g][i].record(st)
+                joint.wait_event(self.ev_out[g][i])
+            self.ev_push[g].record(joint)
         for st in self.s_in + self.s_out + self.s_comp + self.s_join:
             C.wait_stream(st)
         self._barrier()  # every peer's pushes into this rank's out_recv are complete
@@ -337,8 +381,21 @@ def ulysses_bsa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, sha
         if ex is None and exchange == "copy_engine":
             raise ValueError("the copy-engine exchange needs CUDA tensors and an NCCL process group")
         if ex is not None:
-            def compute(qh, kh, vh, o):
-                bsa_attention(qh, kh, vh, shape, sparsity, chunk_thw, sm_scale, topk=topk, rope=rope, out=o)
+            from . import _native
+            from .models.block_sparse_attention import num_selected_blocks
+
+            S = Sl * P
+            _native._geometry(S, shape, chunk_thw)
+            nb = S // (chunk_thw[0] * chunk_thw[1] * chunk_thw[2])
+            k_sel = num_selected_blocks(nb, sparsity) if topk is None else int(topk)
+            scale = 1.0 / math.sqrt(D) if sm_scale is None else sm_scale
+            rope_arg = rope.native_args() if rope is not None else None
+            nbytes = int(_native.lib().bsa_forward_scratch_bytes(B, H // P // G, S, D, *chunk_thw))
+
+            def compute(qh, kh, vh, o, sl):
+                idx, scratch = ex.slot_buffers(sl, nb, k_sel, nbytes)
+                _native.forward(qh, kh, vh, shape, chunk_thw, k_sel, scale, rope=rope_arg, out=o, block_indices=idx,
+                                scratch=scratch)
 
             return ex.run(q, k, v, compute)
     elif exchange != "messages":
