@@ -21,6 +21,7 @@ sample (one head of the config: routing + sparse attention), reported in the sam
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -72,6 +73,16 @@ def _peaks():
 
 
 # ------------------------------------------------------------------------------- clocks
+class NullSampler:
+    """Stand-in for ranks other than 0, whose clock summaries are not printed."""
+
+    def mark(self, on):
+        pass
+
+    def summary(self):
+        return None
+
+
 class ClockSampler:
     """SM clock and throttle reasons of one GPU, polled through NVML every few milliseconds by a host thread
     (falling back to `nvidia-smi -lms 200` when NVML is unavailable).  `mark(True/False)` brackets the timed
@@ -341,8 +352,14 @@ def run_ours(args, cfg):
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(local) as clk:
+    # rank 0 samples its GPU's clocks (its summary is the one printed); the other ranks do not poll NVML
+    with (ClockSampler(local) if rank == 0 else contextlib.nullcontext(NullSampler())) as clk:
         time.sleep(0.02)  # the sampler's first reading lands before the timed region
+        if world > 1:
+            # the ranks left the sampler's start-up at different times: line them up again, so the first
+            # step's barrier does not count one rank's start-up skew as exchange time
+            dist.barrier()
+            torch.cuda.synchronize()
         clk.mark(True)
         t_start.record(stream)
         for i in range(args.steps):
@@ -455,7 +472,8 @@ def run_ours(args, cfg):
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
-            "ms_per_step_stats": {"median": pct(0.5), "p10": pct(0.1), "p90": pct(0.9), "rank": 0},
+            "ms_per_step_stats": {"median": pct(0.5), "p10": pct(0.1), "p90": pct(0.9), "min": per_step[0],
+                                  "max": per_step[-1], "rank": 0},
             "vs_baseline": None, "dtype": {"torch.bfloat16": "bf16", "torch.float16": "f16",
                       "torch.float32": "f32 I/O and routing, f16 attention"}[str(cfg.dtype)],
             "data": "synthetic (seeded; config-2 style per-block offsets)",
