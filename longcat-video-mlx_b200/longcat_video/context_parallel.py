@@ -25,7 +25,8 @@ import torch.distributed as dist
 
 from .models.block_sparse_attention import bsa_attention
 
-__all__ = ["seq_to_heads", "heads_to_seq", "ulysses_bsa_attention", "PeerExchange", "close_exchanges"]
+__all__ = ["seq_to_heads", "heads_to_seq", "ulysses_bsa_attention", "PeerExchange", "close_exchanges",
+           "exchange_copy_plan"]
 
 
 def _world(group) -> int:
@@ -130,6 +131,39 @@ COPY_STREAMS = 1
 COMPUTE_STREAMS = 2
 
 
+def exchange_copy_plan(P: int, r: int, B: int, H: int, Sl: int, D: int, elt: int, G: int, stage, outr, recv_in,
+                       o_slot, nin: int = 1, nout: int = 1):
+    """The copies of one ``PeerExchange`` call on rank r, as bsa_copy_3d rows (dst, dpitch, dslice, src, spitch,
+    sslice, width, height, depth) in bytes.  stage[p] / outr[p]: rank p's stage [3, B, H, S/P, D] and
+    out_recv [B, H, S/P, D] (mapped here); recv_in[slot] [3, B, Hl, S, D] and o_slot[slot] [B, Hl, S, D]: this
+    rank's two input and output slots.  Returns (pull, push): per head group, per copy stream, a list of rows.
+
+    The copy engine pays a fixed cost per call, so a pull moves q, k and v of the group's heads from one peer
+    in one 3-D copy (slices: the tensors; rows: the heads; a row: the peer's token range of one head)."""
+    S, Hg = Sl * P, H // G
+    Hl = Hg // P
+    piece, row = Sl * D * elt, S * D * elt
+    pull, push = [], []
+    for g in range(G):
+        sl = g % 2
+        h0 = g * Hg + r * Hl  # first head of this group that rank r computes
+        ins = [[] for _ in range(nin)]
+        for p in range(P):
+            for b in range(B):
+                src = stage[p] + (b * H + h0) * piece
+                dst = recv_in[sl] + (b * Hl * S + p * Sl) * D * elt
+                ins[(p + r) % nin].append((dst, row, B * Hl * row, src, piece, B * H * piece, piece, Hl, 3))
+        outs = [[] for _ in range(nout)]
+        for p in range(P):
+            for b in range(B):
+                src = o_slot[sl] + (b * Hl * S + p * Sl) * D * elt
+                dst = outr[p] + (b * H + h0) * piece
+                outs[(p + r) % nout].append((dst, piece, piece * Hl, src, row, row * Hl, piece, Hl, 1))
+        pull.append(ins)
+        push.append(outs)
+    return pull, push
+
+
 class PeerExchange:
     """Copy-engine all-to-all for the sequence-parallel BSA call (one per process group and shape).
 
@@ -204,42 +238,18 @@ class PeerExchange:
         self._slot_bufs = {}
 
     def _plan(self):
-        """Every copy of a call, fixed once: the buffers are persistent, so each head group's pulls (peers'
-        stages -> input slot g % 2) and pushes (output slot g % 2 -> peers' out_recv) are lists of copies,
-        one list per copy stream, issued by one host call each (bsa_copy_3d_list).  The copy engine pays a
-        fixed cost per call, so a pull moves q, k and v of the group's heads from one peer in one 3-D copy
-        (slices: the tensors; rows: the heads; a row: the peer's token range of one head)."""
+        """Every copy of a call, fixed once (``exchange_copy_plan``), packed for one host call per stream."""
         import ctypes
-
-        P, r, B, H, Sl, D, S, Hl, Hg, e = (self.P, self.rank, self.B, self.H, self.Sl, self.D, self.S, self.Hl,
-                                            self.Hg, self.elt)
-        piece, row = Sl * D * e, S * D * e
-        nin, nout = len(self.s_in), len(self.s_out)
-        self.pull, self.push = [], []
 
         def pack(rows):
             arr = (ctypes.c_int64 * (9 * max(1, len(rows))))(*[x for rw in rows for x in rw])
             return arr, len(rows)
 
-        for g in range(self.G):
-            sl = g % 2
-            h0 = g * Hg + r * Hl  # first head of this group that this rank computes
-            ins = [[] for _ in range(nin)]
-            dst0 = self.recv_in[sl].data_ptr()
-            for p in range(P):
-                for b in range(B):
-                    src = self.peer_stage[p] + (b * H + h0) * piece       # stage [3, B, H, Sl, D]
-                    dst = dst0 + (b * Hl * S + p * Sl) * D * e            # recv_in [3, B, Hl, S, D]
-                    ins[(p + r) % nin].append((dst, row, B * Hl * row, src, piece, B * H * piece, piece, Hl, 3))
-            outs = [[] for _ in range(nout)]
-            src0 = self.o_slot[sl].data_ptr()
-            for p in range(P):
-                for b in range(B):
-                    src = src0 + (b * Hl * S + p * Sl) * D * e            # o_slot [B, Hl, S, D]
-                    dst = self.peer_outr[p] + (b * H + h0) * piece        # out_recv [B, H, Sl, D]
-                    outs[(p + r) % nout].append((dst, piece, piece * Hl, src, row, row * Hl, piece, Hl, 1))
-            self.pull.append([pack(x) for x in ins])
-            self.push.append([pack(x) for x in outs])
+        pull, push = exchange_copy_plan(self.P, self.rank, self.B, self.H, self.Sl, self.D, self.elt, self.G,
+                                        self.peer_stage, self.peer_outr, [t.data_ptr() for t in self.recv_in],
+                                        [t.data_ptr() for t in self.o_slot], len(self.s_in), len(self.s_out))
+        self.pull = [[pack(x) for x in g] for g in pull]
+        self.push = [[pack(x) for x in g] for g in push]
 
     def slot_buffers(self, sl: int, nb: int, topk: int, scratch_bytes: int):
         """Per-slot routing output and scratch of the compute step (allocated once per size)."""

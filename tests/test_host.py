@@ -6,6 +6,7 @@ import math
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch
 import torch.multiprocessing as mp
@@ -318,3 +319,61 @@ def test_unreadable_views_are_copied_not_refused():
     q = qkv[0]
     assert _native._aligned(q) is q
     assert _native._merge_batch(q) is not q
+
+
+# ------------------------------------------------------------------ the copy-engine exchange's copy plan
+def _apply_copy_3d(arena, row):
+    dst, dpitch, dslice, src, spitch, sslice, width, height, depth = row
+    for z in range(depth):
+        for y in range(height):
+            d0, s0 = dst + z * dslice + y * dpitch, src + z * sslice + y * spitch
+            arena[d0:d0 + width] = arena[s0:s0 + width].copy()
+
+
+@pytest.mark.parametrize("P,B,H,G,nin", [(2, 1, 8, 4, 1), (2, 2, 8, 2, 2), (4, 1, 8, 2, 1), (4, 2, 16, 4, 3),
+                                         (8, 1, 32, 4, 1), (2, 1, 4, 1, 1)])
+def test_exchange_copy_plan_moves_every_piece(P, B, H, G, nin):
+    """``exchange_copy_plan`` (the copies of PeerExchange) restated on one byte arena per rank set: after the
+    pulls of every head group each rank's input slot holds the whole sequence of its heads of the group, and
+    after the pushes every rank's out_recv holds its token range of every head, as seq_to_heads /
+    heads_to_seq define them."""
+    from longcat_video.context_parallel import exchange_copy_plan
+
+    Sl, D, elt = 3, 4, 2
+    S, Hg = Sl * P, H // G
+    Hl = Hg // P
+    # one arena: per rank a stage [3,B,H,Sl,D], an out_recv [B,H,Sl,D], two input slots, two output slots
+    sizes = [3 * B * H * Sl * D, B * H * Sl * D] + [3 * B * Hl * S * D] * 2 + [B * Hl * S * D] * 2
+    base, offs = 0, []
+    for r in range(P):
+        o = []
+        for n in sizes:
+            o.append(base)
+            base += n * elt
+        offs.append(o)
+    arena = np.zeros(base, dtype=np.uint8)
+    view = lambda off, shape: arena[off:off + int(np.prod(shape)) * elt].view(np.uint16).reshape(shape)
+    rng = np.random.default_rng(P * 100 + H)
+    full = rng.integers(1, 60000, size=(3, B, H, S, D), dtype=np.uint16)  # q/k/v of the whole sequence
+    for r in range(P):
+        view(offs[r][0], (3, B, H, Sl, D))[...] = full[:, :, :, r * Sl:(r + 1) * Sl]
+    plans = [exchange_copy_plan(P, r, B, H, Sl, D, elt, G, [offs[p][0] for p in range(P)],
+                                [offs[p][1] for p in range(P)], offs[r][2:4], offs[r][4:6], nin, nin)
+             for r in range(P)]
+    out_full = rng.integers(1, 60000, size=(B, H, S, D), dtype=np.uint16)  # what attention would return
+    for g in range(G):
+        sl = g % 2
+        for r in range(P):
+            for stream in plans[r][0][g]:
+                for row in stream:
+                    _apply_copy_3d(arena, row)
+            heads = [g * Hg + r * Hl + j for j in range(Hl)]
+            got = view(offs[r][2 + sl], (3, B, Hl, S, D))
+            assert np.array_equal(got, full[:, :, heads]), (g, r)
+            view(offs[r][4 + sl], (B, Hl, S, D))[...] = out_full[:, heads]
+        for r in range(P):
+            for stream in plans[r][1][g]:
+                for row in stream:
+                    _apply_copy_3d(arena, row)
+    for r in range(P):
+        assert np.array_equal(view(offs[r][1], (B, H, Sl, D)), out_full[:, :, r * Sl:(r + 1) * Sl]), r
