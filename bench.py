@@ -5,8 +5,9 @@ TFLOP/s = 4*B*H*S*k*64*D / t, as a fraction of bf16 tensor peak).
 
 One step = one full BSA call on synthetic config inputs already resident in HBM: Q and K block
 pooling, routing (bf16 pair split, tcgen05 approximate score keys, per-row selection with exact fp32
-scores in the threshold band, the exact fallback for unsettled rows) and the sparse tcgen05 attention
-(7 kernel launches).
+scores in the threshold band, the exact fallback for unsettled rows) and the sparse tcgen05 attention,
+through the engine's forward entry (6 kernel launches: the bf16 pair split of the routing runs inside
+the two pool kernels).
 At N > 1 (torchrun, one rank per GPU, NCCL) every rank holds a sequence shard of Q/K/V for all
 32 heads; a step is the sequence -> heads exchange, the BSA call on its 32/N heads and the
 exchange back, pipelined over head groups (ulysses_bsa_attention).
@@ -320,17 +321,25 @@ def run_ours(args, cfg):
     stream = torch.cuda.current_stream(dev)
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
 
+    scratch_by_heads = {}
+
     def local_call(qh, kh, vh, i=None):
-        """One BSA call on whole-sequence heads, kernel by kernel, with events around routing and attention."""
+        """One BSA call on whole-sequence heads through the engine's forward entry (the path of
+        bsa_attention), with events before it, between routing and attention (the engine's phase-event
+        hook) and after it."""
+        heads = int(qh.shape[1])
+        if heads not in scratch_by_heads:
+            nbytes = int(_native.lib().bsa_forward_scratch_bytes(B, heads, S, D, *cfg.chunk))
+            scratch_by_heads[heads] = torch.empty((nbytes,), device=dev, dtype=torch.uint8)
         if i is not None:
             ev[i][0].record(stream)
-        qp, q_rot = _native.mean_pool(qh, cfg.shape, cfg.chunk, rope=rope_args)
-        kp, k_rot = _native.mean_pool(kh, cfg.shape, cfg.chunk, rope=rope_args)
-        ix, _ = _native.score_topk(qp, kp, cfg.topk)
-        if i is not None:
-            ev[i][1].record(stream)
-        o = _native.attention_indices(q_rot if rope else qh, k_rot if rope else kh, vh, ix, cfg.shape, cfg.chunk,
-                                      scale, out=out_h)
+            _native.set_phase_event(ev[i][1])
+        try:
+            o = _native.forward(qh, kh, vh, cfg.shape, cfg.chunk, cfg.topk, scale, rope=rope_args, out=out_h[:, :heads],
+                                block_indices=idx[:, :heads], scratch=scratch_by_heads[heads])
+        finally:
+            if i is not None:
+                _native.set_phase_event(None)
         if i is not None:
             ev[i][2].record(stream)
         return o
@@ -498,7 +507,7 @@ def run_ours(args, cfg):
             "e2e": {"value": cfg.sparse_flops() / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             # per step: pool Q, pool K, pair split, score keys, select, fallback, attention
-            "gpu_launches": 7 * args.steps,
+            "gpu_launches": 6 * args.steps,
             "clocks": clk.summary(),
         }
         if cpu:

@@ -159,6 +159,12 @@ int bsa_forward_qknorm(const void* q, const void* k, const void* v, int dtype, i
                        const void* k_norm_weight, float norm_eps, void* q_rot, void* k_rot, void* scratch,
                        int32_t* block_indices, void* out, const int64_t* out_strides, int sm_reserve, void* stream);
 
+/* bsa_set_phase_event: profiling hook, no counterpart in the reference.  `event` (a cudaEvent_t, or NULL to
+ * stop) is recorded on the call's stream between the routing launches and the attention launch of every
+ * later bsa_forward* call made by the calling host thread, so a caller can time the two phases of one
+ * call with CUDA events.  The event must outlive those calls. */
+int bsa_set_phase_event(void* event);
+
 /* bsa_forward without caller-provided scratch -- no counterpart in the reference (MLX manages
  * memory itself); it exists for callers that cannot allocate device memory where they call
  * attention (a region whose memory is fixed in advance, an embedder that owns the whole device

@@ -134,6 +134,10 @@ int make_pair_map(CUtensorMap* m, const void* base, int nb, int BH) {
 }
 
 // ------------------------------------------------------------------ plans: validated, ready to launch
+// Profiling hook of bsa_set_phase_event: recorded between the routing and the attention launches of
+// the forward calls made by this host thread.
+thread_local cudaEvent_t t_phase_event = nullptr;
+
 struct PoolPlan {
   bsa::PoolArgs a;
   CUtensorMap map;
@@ -392,6 +396,11 @@ int bsa_attention_indices_ex(const void* q, const void* k, const void* v, const 
 
 // Scratch of bsa_forward: pooled Q and K (fp32, [B*H, nb, D] each, padded to 256 bytes), then the
 // routing scratch (bsa_route_topk) where routing supports the size, else the fp32 score matrix.
+int bsa_set_phase_event(void* event) {
+  t_phase_event = static_cast<cudaEvent_t>(event);
+  return BSA_OK;
+}
+
 int64_t bsa_forward_scratch_bytes(int B, int H, int S, int D, int cT, int cH, int cW) {
   const int n = cT * cH * cW;
   if (n <= 0 || B <= 0 || H <= 0 || S <= 0 || D <= 0) return 0;
@@ -451,6 +460,9 @@ int forward_impl(const void* q, const void* k, const void* v, int dtype, int B, 
   bsa::RouteArgs ra;
   ra.qp = qp; ra.kp = kp; ra.BH = B * H; ra.nb = nb; ra.D = D; ra.topk = topk;
   ra.idx = block_indices; ra.scratch = rest; ra.make_pair_map = make_pair_map;
+  __nv_bfloat16* split_hl = nullptr;
+  float* split_nrm = nullptr;
+  float* split_nkmax = nullptr;
   bsa::ScoreArgs sa;
   sa.qp = qp; sa.kp = kp; sa.BH = B * H; sa.nq = nb; sa.nk = nb; sa.D = D; sa.topk = topk;
   sa.idx = block_indices; sa.ldc = static_cast<int>(score_ld(nb));
@@ -467,12 +479,27 @@ int forward_impl(const void* q, const void* k, const void* v, int dtype, int B, 
   }
   if (rc) return rc;
   // ---- launches
+  if (route) {
+    // the pool kernels also write the routing's split (bf16 pairs, norm bounds) while each pooled row is
+    // in registers; the per-head maximum key norm and the fallback count start at 0 before the pool of K
+    if (bsa::route_split_targets(rest, B * H, nb, &split_hl, &split_nrm, &split_nkmax,
+                                 static_cast<cudaStream_t>(stream)) != BSA_OK)
+      return cuda_fail("routing scratch reset");
+    pq.a.split_hl = pk.a.split_hl = split_hl;
+    pq.a.split_nrm = pk.a.split_nrm = split_nrm;
+    pq.a.split_nkmax = pk.a.split_nkmax = split_nkmax;
+    pq.a.split_which = 0;
+    pk.a.split_which = 1;
+    ra.split_done = 1;
+  }
   if ((rc = pool_run(pq, stream))) return rc;
   if ((rc = pool_run(pk, stream))) return rc;
   rc = route ? bsa::launch_route(ra, static_cast<cudaStream_t>(stream))
              : bsa::launch_score_topk(sa, static_cast<cudaStream_t>(stream));
   if (rc == BSA_ERR_CUDA) return cuda_fail("routing kernel launch");
   if (rc) return rc == BSA_ERR_ARG ? rc : fail(rc, "routing: unsupported sizes (nb=%d)", nb);
+  if (t_phase_event && cudaEventRecord(t_phase_event, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return cuda_fail("phase event record");
   return attn_run(pa, stream);
 }
 }  // namespace

@@ -2,6 +2,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include "../../include/bsa_b200.h"
 
@@ -25,6 +26,12 @@ struct PoolArgs {
   // optional fused RMSNorm_FP32 (blocks.py:55-73) before the RoPE: weight [D] in x's dtype (nullable)
   const void* norm_w;
   float norm_eps;
+  // optional fused routing split (the work of the routing's split step, done while the pooled row is in
+  // registers): bf16 hi/lo pairs [4][B*H*nb][128], row norm bounds [2][B*H*nb], per-head max key norm
+  __nv_bfloat16* split_hl = nullptr;  // nullable
+  float* split_nrm = nullptr;
+  float* split_nkmax = nullptr;
+  int split_which = 0;                // 0: this is Q, 1: this is K
 };
 int launch_pool(const PoolArgs& a, cudaStream_t stream);
 
@@ -52,7 +59,12 @@ struct RouteArgs {
   void* scratch;         // route_scratch_bytes(BH, nb), 256-byte aligned
   // builds a 3-D bf16 map (d = 128, block = nb, b*h = BH) with 64 x 128 boxes over one pair array
   int (*make_pair_map)(CUtensorMap* m, const void* base, int nb, int BH);
+  int split_done = 0;    // the pool kernels already wrote the split (route_split_targets)
 };
+// Where the split step writes inside the routing scratch; zeroes the per-head max key norm and the
+// fallback-row count on `stream` (they must start at 0 before the pool of K runs).
+int route_split_targets(void* scratch, int BH, int nb, __nv_bfloat16** hl, float** nrm, float** nkmax,
+                        cudaStream_t stream);
 bool route_supported(int nb, int D);
 int64_t route_scratch_bytes(int BH, int nb);
 int launch_route(const RouteArgs& a, cudaStream_t stream);

@@ -662,28 +662,62 @@ int64_t route_scratch_bytes(int BH, int nb) {
 
 bool route_supported(int nb, int D) { return nb >= 1 && nb <= 3072 && D >= 8 && D <= 128 && D % 8 == 0; }
 
+namespace {
+struct RouteLayout {
+  __nv_bfloat16* hl;
+  float* nrm;
+  float* nkmax;  // [BH], then the fallback-row count
+  int* fb_count;
+  int* fb_rows;
+  uint16_t* keys;
+};
+RouteLayout route_layout(void* scratch, int BH, int nb) {
+  const int64_t rows = static_cast<int64_t>(BH) * nb;
+  RouteLayout l;
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  l.hl = reinterpret_cast<__nv_bfloat16*>(base);
+  base += up256(4ll * rows * route::kDP * 2);
+  l.nrm = reinterpret_cast<float*>(base);
+  base += up256(2ll * rows * 4);
+  l.nkmax = reinterpret_cast<float*>(base);
+  l.fb_count = reinterpret_cast<int*>(l.nkmax + BH);
+  base += up256((static_cast<int64_t>(BH) + 4) * 4);
+  l.fb_rows = reinterpret_cast<int*>(base);
+  base += up256(rows * 4);
+  l.keys = reinterpret_cast<uint16_t*>(base);
+  return l;
+}
+}  // namespace
+
+int route_split_targets(void* scratch, int BH, int nb, __nv_bfloat16** hl, float** nrm, float** nkmax,
+                        cudaStream_t stream) {
+  const RouteLayout l = route_layout(scratch, BH, nb);
+  *hl = l.hl;
+  *nrm = l.nrm;
+  *nkmax = l.nkmax;
+  return cudaMemsetAsync(l.nkmax, 0, (static_cast<size_t>(BH) + 4) * 4, stream) == cudaSuccess ? BSA_OK
+                                                                                                : BSA_ERR_CUDA;
+}
+
 int launch_route(const RouteArgs& a, cudaStream_t stream) {
   using namespace route;
   if (!route_supported(a.nb, a.D) || !a.scratch) return BSA_ERR_SHAPE;
   const int rows = a.BH * a.nb;
   const int64_t ldk = (static_cast<int64_t>(a.nb) + 7) & ~int64_t(7);
-  uint8_t* base = static_cast<uint8_t*>(a.scratch);
-  __nv_bfloat16* hl = reinterpret_cast<__nv_bfloat16*>(base);
-  base += up256(4ll * rows * kDP * 2);
-  float* nrm = reinterpret_cast<float*>(base);
-  base += up256(2ll * rows * 4);
-  float* nkmax = reinterpret_cast<float*>(base);
-  int* fb_count = reinterpret_cast<int*>(nkmax + a.BH);
-  base += up256((static_cast<int64_t>(a.BH) + 4) * 4);
-  int* fb_rows = reinterpret_cast<int*>(base);
-  base += up256(static_cast<int64_t>(rows) * 4);
-  uint16_t* keys = reinterpret_cast<uint16_t*>(base);
+  const RouteLayout lay = route_layout(a.scratch, a.BH, a.nb);
+  __nv_bfloat16* hl = lay.hl;
+  float* nrm = lay.nrm;
+  float* nkmax = lay.nkmax;
+  int* fb_count = lay.fb_count;
+  int* fb_rows = lay.fb_rows;
+  uint16_t* keys = lay.keys;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return BSA_ERR_CUDA;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // 1. split (+ the per-head maximum key norm and the fallback count, which start at 0)
-  if (cudaMemsetAsync(nkmax, 0, (static_cast<size_t>(a.BH) + 4) * 4, stream) != cudaSuccess) return BSA_ERR_CUDA;
-  {
+  // 1. split (+ the per-head maximum key norm and the fallback count, which start at 0), unless the pool
+  //    kernels did it
+  if (!a.split_done) {
+    if (cudaMemsetAsync(nkmax, 0, (static_cast<size_t>(a.BH) + 4) * 4, stream) != cudaSuccess) return BSA_ERR_CUDA;
     long long grid = (2ll * rows + 7) / 8;
     if (grid > static_cast<long long>(sms) * 16) grid = static_cast<long long>(sms) * 16;
     split_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(a.qp, a.kp, rows, a.nb, a.D, hl, nrm, nkmax);

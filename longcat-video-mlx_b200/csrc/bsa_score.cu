@@ -47,7 +47,45 @@ struct Geo {
   int map3;  // the TMA-ring kernel's map is 3-D (d, s, b*h): blocks are contiguous token runs
   const void* nw;  // nullable: RMSNorm weight [D] in the input dtype (fused q/k norm)
   float eps;
+  __nv_bfloat16* hl;  // nullable: fused routing split (see split_row)
+  float* nrm;
+  float* nkmax;
+  int which;          // 0: Q, 1: K
 };
+
+// The routing's split step for one pooled row, done while the row is in registers (route::split_kernel in
+// bsa_route.cu does the same from memory when the pool kernels do not): bf16 pairs hi = bf16(x),
+// lo = bf16(x - hi) padded to 128 columns, an upper bound of the row's l2 norm (+inf for values the
+// routing's error bound does not cover: non-finite, above 2^60 or below 2^-60 in magnitude), and for K the
+// per-head maximum of those bounds.  One warp per row; lane l holds d = 4l .. 4l+3 (zeros past D).
+__device__ __forceinline__ void split_row(const Geo& g, int bh, int blk, const float (&x)[4], int lane) {
+  const long long rows = static_cast<long long>(g.B) * g.H * g.nb;
+  const long long row = static_cast<long long>(bh) * g.nb + blk;
+  __nv_bfloat16 hi[4], lo[4];
+  float n2 = 0.f;
+  bool extreme = false;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    hi[e] = __float2bfloat16_rn(x[e]);
+    lo[e] = __float2bfloat16_rn(__fsub_rn(x[e], __bfloat162float(hi[e])));
+    n2 = fmaf(x[e], x[e], n2);
+    const float a = fabsf(x[e]);
+    extreme |= !(a <= 1.152921504606847e18f) || (a != 0.f && a < 8.673617379884035e-19f);  // 2^60, 2^-60
+  }
+  __nv_bfloat16* dh = g.hl + (static_cast<long long>(2 * g.which) * rows + row) * 128 + 4 * lane;
+  __nv_bfloat16* dl = g.hl + (static_cast<long long>(2 * g.which + 1) * rows + row) * 128 + 4 * lane;
+  *reinterpret_cast<uint2*>(dh) = *reinterpret_cast<const uint2*>(hi);
+  *reinterpret_cast<uint2*>(dl) = *reinterpret_cast<const uint2*>(lo);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, off);
+  extreme = __any_sync(0xffffffffu, extreme);
+  if (lane == 0) {
+    // sqrt of an fp32 sum of 128 squares: relative error far below 2^-10, so the bound holds
+    const float n = extreme ? INFINITY : __fmul_ru(sqrtf(n2), 1.0009765625f);
+    g.nrm[static_cast<long long>(g.which) * rows + row] = n;
+    if (g.which) atomicMax(reinterpret_cast<int*>(g.nkmax) + bh, __float_as_int(n));  // n >= 0
+  }
+}
 
 // Four consecutive d values of one token row: 8 bytes (fp16/bf16) or 16 bytes (fp32).
 __device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
@@ -236,11 +274,10 @@ __global__ void __launch_bounds__(kThreads, kRope ? 3 : 4)
 #pragma unroll
       for (int e = 0; e < 4; ++e) tot[e] = lvl[0][e];
     }
-    if (dact) {
-      const float out[4] = {__fmul_rn(tot[0], inv_n), __fmul_rn(tot[1], inv_n), __fmul_rn(tot[2], inv_n),
-                            __fmul_rn(tot[3], inv_n)};
-      store4(pooled + (static_cast<long long>(bh) * g.nb + blk) * g.D + d0, out);
-    }
+    const float out[4] = {dact ? __fmul_rn(tot[0], inv_n) : 0.f, dact ? __fmul_rn(tot[1], inv_n) : 0.f,
+                          dact ? __fmul_rn(tot[2], inv_n) : 0.f, dact ? __fmul_rn(tot[3], inv_n) : 0.f};
+    if (dact) store4(pooled + (static_cast<long long>(bh) * g.nb + blk) * g.D + d0, out);
+    if (g.hl) split_row(g, bh, blk, out, lane);
   }
 }
 // ------------------------------------------------------------------------ pooling through a TMA ring
@@ -418,11 +455,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&rs.empty[slot]);  // the slot's rows are in registers / written out
-      if (dact) {
-        const float out[4] = {__fmul_rn(tot[0], inv_n), __fmul_rn(tot[1], inv_n), __fmul_rn(tot[2], inv_n),
-                              __fmul_rn(tot[3], inv_n)};
-        store4(pooled + (static_cast<long long>(bh) * g.nb + blk) * g.D + d0, out);
-      }
+      const float out[4] = {dact ? __fmul_rn(tot[0], inv_n) : 0.f, dact ? __fmul_rn(tot[1], inv_n) : 0.f,
+                            dact ? __fmul_rn(tot[2], inv_n) : 0.f, dact ? __fmul_rn(tot[3], inv_n) : 0.f};
+      if (dact) store4(pooled + (static_cast<long long>(bh) * g.nb + blk) * g.D + d0, out);
+      if (g.hl) split_row(g, bh, blk, out, lane);
     }
   }
 }
@@ -441,6 +477,7 @@ int launch_pool(const PoolArgs& a, cudaStream_t stream) {
   g.rT = a.rope_T; g.rH = a.rope_H; g.rW = a.rope_W;
   g.map3 = a.map3;
   g.nw = a.norm_w; g.eps = a.norm_eps;
+  g.hl = a.split_hl; g.nrm = a.split_nrm; g.nkmax = a.split_nkmax; g.which = a.split_which;
   if (n < 1 || n > 64 || (n & (n - 1)) || a.D > 128 || a.D % 4) return BSA_ERR_SHAPE;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);

@@ -61,6 +61,7 @@ _SIGNATURES = {
     "bsa_copy_3d": ([_vp, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                      ctypes.c_int64, ctypes.c_int64, _vp], _i),
     "bsa_copy_3d_list": ([_vp, _i, _vp], _i),
+    "bsa_set_phase_event": ([_vp], _i),
     "bsa_attention_indices_ex": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i,
                                   _i, _i, _i, _f, _vp, _c_i64p, _i, _vp], _i),
     "bsa_forward_ex": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _c_i64p, _c_i64p, _c_i64p, _i, _i, _i, _i, _i, _i, _i, _f,
@@ -449,6 +450,17 @@ def ipc_close(ptr: int) -> None:
 def copy_2d(dst: int, dpitch: int, src: int, spitch: int, width: int, height: int, stream) -> None:
     """`height` rows of `width` bytes between any local / mapped-peer addresses, on `stream`."""
     _check(lib().bsa_copy_2d(dst, dpitch, src, spitch, width, height, stream.cuda_stream), "bsa_copy_2d")
+
+
+def set_phase_event(event) -> None:
+    """Record `event` (a torch.cuda.Event, or None to stop) between the routing and the attention launches
+    of this thread's later forward calls (profiling: the two phases of one call)."""
+    handle = None
+    if event is not None:
+        if not event.cuda_event:  # torch creates the CUDA event at its first record
+            event.record(torch.cuda.current_stream())
+        handle = event.cuda_event
+    _check(lib().bsa_set_phase_event(handle), "bsa_set_phase_event")
 
 
 def copy_3d_list(desc, n: int, stream) -> None:
