@@ -42,7 +42,7 @@ METRIC = "BSA sparse TFLOP/s (4*B*H*S*k*64*D per call) at the 720p refinement sh
 UNIT = "TFLOP/s"
 # DRAM bytes (read + write) of one attention launch per (batch, head) at the config-2 shape: ncu
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch on 4 heads of config 2 (inputs 265 MB, above
-# the L2), 339.0 + 77.7 MB (profiles/bsa_kernels_config2_h4_full.md); the traffic is per head.
+# the L2), 339.0 + 77.7 MB; the traffic is per head.
 ATTN_DRAM_BYTES_PER_HEAD = {"config2": (338.954496e6 + 77.703936e6) / 4}
 # L2 -> shared-memory rate of TMA tensor gathers alone: 148 CTAs, each keeping 192 KB of random 16 KB K+V
 # blocks (two 64 x 64 bf16 boxes each, 128B swizzle) of one head's 44 MB working set in flight and
