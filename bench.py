@@ -382,7 +382,16 @@ def run_ours(args, cfg):
     torch.cuda.synchronize()
     total_ms = t_start.elapsed_time(t_end)
     bounds = step_ev + [t_end]
-    per_step = sorted(bounds[i].elapsed_time(bounds[i + 1]) for i in range(args.steps))
+    steps_ms = [bounds[i].elapsed_time(bounds[i + 1]) for i in range(args.steps)]
+    rank_totals = [total_ms]
+    if world > 1:
+        # per step, the slowest rank; and every rank's total (the reported value takes the largest)
+        st = torch.tensor(steps_ms + [total_ms], device=dev, dtype=torch.float64)
+        gathered = [torch.empty_like(st) for _ in range(world)]
+        dist.all_gather(gathered, st)
+        steps_ms = torch.stack(gathered)[:, :-1].max(dim=0).values.tolist()
+        rank_totals = [float(g[-1]) for g in gathered]
+    per_step = sorted(steps_ms)
     pct = lambda q: per_step[min(len(per_step) - 1, int(q * (len(per_step) - 1) + 0.5))]
     if world > 1:
         # kernel breakdown for the roofline: the same local call on this rank's H/P whole-sequence
@@ -482,7 +491,8 @@ def run_ours(args, cfg):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
             "ms_per_step_stats": {"median": pct(0.5), "p10": pct(0.1), "p90": pct(0.9), "min": per_step[0],
-                                  "max": per_step[-1], "rank": 0},
+                                  "max": per_step[-1], "ranks": "max over ranks per step",
+                                  "rank_totals_ms": [round(t, 3) for t in rank_totals]},
             "vs_baseline": None, "dtype": {"torch.bfloat16": "bf16", "torch.float16": "f16",
                       "torch.float32": "f32 I/O and routing, f16 attention"}[str(cfg.dtype)],
             "data": "synthetic (seeded; config-2 style per-block offsets)",
@@ -540,6 +550,8 @@ def main(argv=None):
                     help="N>1: all-to-all implementation (default: copy engines where they apply)")
     ap.add_argument("--head-groups", type=int, default=None,
                     help="N>1: head groups of the pipelined exchange (default: library default)")
+    ap.add_argument("--copy-streams", type=int, default=None,
+                    help="N>1: copy streams per direction of the copy-engine exchange (default: library default)")
     ap.add_argument("--heads", type=int, default=None,
                     help="override the head count (small cases for profiling; not a bench line)")
     args = ap.parse_args(argv)
@@ -552,6 +564,10 @@ def main(argv=None):
         import dataclasses
 
         cfg = dataclasses.replace(cfg, H=args.heads)
+    if args.copy_streams:
+        from longcat_video import context_parallel
+
+        context_parallel.COPY_STREAMS = args.copy_streams
     if args.impl == "reference":
         return run_reference(args, cfg)
     return run_ours(args, cfg)
