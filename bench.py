@@ -364,12 +364,12 @@ def run_ours(args, cfg):
     # rank 0 samples its GPU's clocks (its summary is the one printed); the other ranks do not poll NVML
     with (ClockSampler(local) if rank == 0 else contextlib.nullcontext(NullSampler())) as clk:
         time.sleep(0.02)  # the sampler's first reading lands before the timed region
+        clk.mark(True)  # (rank 0 reads NVML here: before the ranks line up, so that read is not timed)
         if world > 1:
             # the ranks left the sampler's start-up at different times: line them up again, so the first
             # step's barrier does not count one rank's start-up skew as exchange time
             dist.barrier()
             torch.cuda.synchronize()
-        clk.mark(True)
         t_start.record(stream)
         for i in range(args.steps):
             step_ev[i].record(stream)
