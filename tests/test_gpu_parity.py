@@ -520,6 +520,28 @@ def test_route_wide_rows_take_the_radix_select(cuda):
         _route_vs_oracle(cuda, qp, kp, k)
 
 
+def test_phase_event_splits_one_forward_call(cuda):
+    """bsa_set_phase_event: the event lands between the routing and the attention launches of a forward call
+    (both phases take time), the call's results are those of a call without it, and clearing it stops it."""
+    from longcat_video import _native
+
+    B, H, S, D = 1, 2, 4096, 128
+    q, k, v = (_rand((B, H, S, D), torch.bfloat16, 150 + i, cuda) for i in range(3))
+    ref, ref_idx = _native.forward(q, k, v, (1, 1, S), (1, 1, 64), 8, D ** -0.5)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record()
+    _native.set_phase_event(e1)
+    try:
+        out, idx = _native.forward(q, k, v, (1, 1, S), (1, 1, 64), 8, D ** -0.5)
+    finally:
+        _native.set_phase_event(None)
+    e2.record()
+    torch.cuda.synchronize()
+    assert _native.device_error(clear=True) == 0
+    assert e0.elapsed_time(e1) > 0 and e1.elapsed_time(e2) > 0
+    assert torch.equal(idx, ref_idx) and torch.equal(out, ref)
+
+
 def test_cond_branch_through_the_engine(cuda):
     """attention.py:203-223 on the GPU: with conditioning latents the cond frames run BSA on the engine over
     (num_cond_latents, H, W) and the noise queries attend densely to cond + noise keys.  Each branch is
