@@ -290,7 +290,8 @@ __device__ __forceinline__ float exact_score(const float* q, const float* __rest
 }
 
 // The same chain for two rows at once (row1 may be null), 16 d values per round: every load of a
-// round is issued before its first fma, so a round costs one L2 latency instead of four.
+// round is issued before its first fma, so a round costs one L2 latency instead of four.  q is a 16-byte
+// aligned row in shared memory.
 __device__ __forceinline__ void exact_score2(const float* q, const float* __restrict__ r0, const float* __restrict__ r1,
                                              int D, float& s0, float& s1) {
   float a0 = 0.f, a1 = 0.f;
@@ -306,10 +307,11 @@ __device__ __forceinline__ void exact_score2(const float* q, const float* __rest
     for (int c = 0; c < 4; ++c) {
       const int d = d0 + 4 * c;
       if (d < D) {
-        a0 = fmaf(q[d], k0[c].x, a0); a0 = fmaf(q[d + 1], k0[c].y, a0);
-        a0 = fmaf(q[d + 2], k0[c].z, a0); a0 = fmaf(q[d + 3], k0[c].w, a0);
-        a1 = fmaf(q[d], k1[c].x, a1); a1 = fmaf(q[d + 1], k1[c].y, a1);
-        a1 = fmaf(q[d + 2], k1[c].z, a1); a1 = fmaf(q[d + 3], k1[c].w, a1);
+        const float4 qv = *reinterpret_cast<const float4*>(q + d);  // q: 16-byte aligned shared memory
+        a0 = fmaf(qv.x, k0[c].x, a0); a0 = fmaf(qv.y, k0[c].y, a0);
+        a0 = fmaf(qv.z, k0[c].z, a0); a0 = fmaf(qv.w, k0[c].w, a0);
+        a1 = fmaf(qv.x, k1[c].x, a1); a1 = fmaf(qv.y, k1[c].y, a1);
+        a1 = fmaf(qv.z, k1[c].z, a1); a1 = fmaf(qv.w, k1[c].w, a1);
       }
     }
   }
