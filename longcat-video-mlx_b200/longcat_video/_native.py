@@ -28,6 +28,7 @@ BSA_ERR_TIMEOUT = 6
 BSA_ERR_ARG = 7
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+_phase = threading.local()  # set_phase_event's event of this host thread
 
 _lib = None
 _lock = threading.Lock()
@@ -342,6 +343,9 @@ def _forward_f32(q, k, v, shape, chunk_thw, topk, sm_scale, rope, out, block_ind
     if block_indices is not None:
         block_indices.copy_(idx)
         idx = block_indices
+    ev = getattr(_phase, "event", None)
+    if ev is not None:
+        ev.record(torch.cuda.current_stream(q.device))
     o16 = torch.empty((B, H, S, D), device=q.device, dtype=torch.float16)
     qh, kh, vh = (t.to(torch.float16) for t in (qr, kr, v))
     _attention_ex(qh, kh, vh, idx, shape, chunk_thw, sm_scale, o16, sm_reserve)
@@ -461,6 +465,7 @@ def set_phase_event(event) -> None:
             event.record(torch.cuda.current_stream())
         handle = event.cuda_event
     _check(lib().bsa_set_phase_event(handle), "bsa_set_phase_event")
+    _phase.event = event  # the fp32 path (routing and attention as separate calls) records it here
 
 
 def copy_3d_list(desc, n: int, stream) -> None:
