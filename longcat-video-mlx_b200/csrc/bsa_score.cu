@@ -126,7 +126,7 @@ __device__ __forceinline__ void store4(float* p, const float (&v)[4]) {
 // rows), so the order is fixed and needs no shared memory or barrier.  Each row's token offset
 // inside a block is the same for every block and is tabled once per CTA.
 template <typename T, bool kRope>
-__global__ void __launch_bounds__(kThreads, kRope ? 3 : 4)
+__global__ void __launch_bounds__(kThreads, kRope ? 2 : 4)
     pool_kernel(const T* __restrict__ x, T* xr, float* pooled, Geo g) {
   __shared__ long long roff[64];  // token offset of row r from the block's first token, (ct, ch, cw) order
   const int tid = threadIdx.x;
@@ -206,6 +206,26 @@ __global__ void __launch_bounds__(kThreads, kRope ? 3 : 4)
         if (r0 + i < g.n && dact) load4(base + (tok0 + roff[r0 + i]) * g.ss, v[i]);
         else v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.f;
       }
+      // this group's RoPE table entries, all loads issued before the first use (one latency per 8 rows)
+      float rc[8][2], rsn[8][2];
+      if (kRope && g.rope) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = r0 + i;
+          // this row's position on the RoPE grid, computed by lane r % 32 at the start of the block
+          const int src = r & 31;
+          const int pt = __shfl_sync(0xffffffffu, r < 32 ? posA0 : posA1, src);
+          const int pb = __shfl_sync(0xffffffffu, r < 32 ? posB0 : posB1, src);
+          const int pax[3] = {pt, pb >> 16, pb & 0xffff};
+#pragma unroll
+          for (int pr = 0; pr < 2; ++pr) {
+            const int pos = pax[rax[pr]];
+            const bool live = dact && r < g.n;
+            rc[i][pr] = live ? __ldg(rcos[pr] + pos * rstride[pr]) : 0.f;
+            rsn[i][pr] = live ? __ldg(rsin[pr] + pos * rstride[pr]) : 0.f;
+          }
+        }
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int r = r0 + i;
@@ -230,18 +250,12 @@ __global__ void __launch_bounds__(kThreads, kRope ? 3 : 4)
             }
           }
           if (g.rope) {
-            // this row's position on the RoPE grid, computed by lane r % 32 at the start of the block
-            const int src = r & 31;
-            const int pt = __shfl_sync(0xffffffffu, r < 32 ? posA0 : posA1, src);
-            const int pb = __shfl_sync(0xffffffffu, r < 32 ? posB0 : posB1, src);
-            const int pax[3] = {pt, pb >> 16, pb & 0xffff};
             if (dact) {
               // rotate 2 pairs: (x0, x1) -> (x0*cos - x1*sin, x1*cos + x0*sin), fp32, no fma
 #pragma unroll
               for (int pr = 0; pr < 2; ++pr) {
-                const int pos = pax[rax[pr]];
-                const float cs = __ldg(rcos[pr] + pos * rstride[pr]);
-                const float sn = __ldg(rsin[pr] + pos * rstride[pr]);
+                const float cs = rc[i][pr];
+                const float sn = rsn[i][pr];
                 const float a = v[i][2 * pr], bb = v[i][2 * pr + 1];
                 v[i][2 * pr] = __fadd_rn(__fmul_rn(a, cs), __fmul_rn(-bb, sn));
                 v[i][2 * pr + 1] = __fadd_rn(__fmul_rn(bb, cs), __fmul_rn(a, sn));
