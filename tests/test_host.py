@@ -193,7 +193,7 @@ def test_ulysses_head_group_pipeline_gloo_world2(groups):
 def test_head_group_choice():
     from longcat_video.context_parallel import _head_groups
 
-    assert _head_groups(32, 2, None) == 4 and _head_groups(32, 8, None) == 4
+    assert _head_groups(32, 2, None) == 2 and _head_groups(32, 4, None) == 2 and _head_groups(32, 8, None) == 4
     assert _head_groups(8, 8, None) == 1
     assert _head_groups(32, 8, 3) == 2  # 32/3 does not split; 2 groups of 16 heads do
     assert _head_groups(24, 8, 2) == 1  # 12 heads per group do not split over 8 ranks
