@@ -169,7 +169,7 @@ int bsa_set_phase_event(void* event);
  * memory itself); it exists for callers that cannot allocate device memory where they call
  * attention (a region whose memory is fixed in advance, an embedder that owns the whole device
  * budget, a host binding without a device allocator).  Same arguments and results as bsa_forward
- * minus `scratch`: the pooled Q/K and score scratch comes from an array compiled into the library, of
+ * minus `scratch`: the pooled Q/K and routing scratch comes from an array compiled into the library, of
  * BSA_NOALLOC_SCRATCH_BYTES per GPU that loads the library, held until the process exits.
  * Calls that would need more (bsa_forward_scratch_bytes() > BSA_NOALLOC_SCRATCH_BYTES) return
  * BSA_ERR_SHAPE.  Nothing is allocated: no cudaMalloc, cudaFree or allocating library routine.
@@ -178,8 +178,9 @@ int bsa_set_phase_event(void* event);
  * capture.  A device reset (cudaDeviceReset) is not supported: the cached address would be stale.
  * Every call on a device shares the one array: calls whose kernels overlap on the GPU (different
  * streams, or concurrent host threads) race on it and must be serialised by the caller.  The array
- * serves calls with 4*B*H*nb*(2*D + round_up(nb, 4)) <= BSA_NOALLOC_SCRATCH_BYTES (nb = S/64), i.e.
- * small shapes; the 720p benchmark shapes need far more and are refused. */
+ * serves calls with bsa_forward_scratch_bytes(B, H, S, D, cT, cH, cW) <= BSA_NOALLOC_SCRATCH_BYTES, i.e.
+ * small shapes (about B*H*nb*(8*D + 2*nb + 1100) bytes, nb = S/64); the 720p benchmark shapes need far
+ * more and are refused. */
 #define BSA_NOALLOC_SCRATCH_BYTES (16u << 20)
 int bsa_forward_noalloc(const void* q, const void* k, const void* v, int dtype, int B, int H, int S, int D,
                         const int64_t* q_strides, const int64_t* k_strides, const int64_t* v_strides, int T, int Hl,
