@@ -33,13 +33,15 @@ def main():
         Sl = S // world
         sh = slice(rank * Sl, (rank + 1) * Sl)
         qs, ks, vs = (x[:, :, sh].contiguous() for x in (q, k, v))
-        for exchange in ("copy_engine", "messages"):
+        # the copy-engine exchange with its default head groups and with one and four groups (other copy plans)
+        for exchange, groups in (("copy_engine", None), ("copy_engine", 1), ("copy_engine", 4), ("messages", None)):
             for _ in range(2):  # second call reuses the exchange's buffers
                 got = ulysses_bsa_attention(qs, ks, vs, shape, chunk_thw=chunk, topk=topk, rope=rope,
-                                            exchange=exchange)
+                                            exchange=exchange, head_groups=groups)
                 same = torch.equal(got, want[:, :, sh])
                 if not same:
-                    print(f"rank {rank}: mismatch B={B} H={H} shape={shape} exchange={exchange}", flush=True)
+                    print(f"rank {rank}: mismatch B={B} H={H} shape={shape} exchange={exchange} groups={groups}",
+                          flush=True)
                 ok &= same
     close_exchanges()
     flag = torch.tensor([0 if ok else 1], device=dev)
