@@ -324,6 +324,11 @@ def test_unreadable_views_are_copied_not_refused():
 # ------------------------------------------------------------------ the copy-engine exchange's copy plan
 def _apply_copy_3d(arena, row):
     dst, dpitch, dslice, src, spitch, sslice, width, height, depth = row
+    # the extents bsa_copy_3d accepts (bsa_xfer.cu): pitches hold a row, slice pitches whole rows of a slice
+    assert 0 < width <= min(dpitch, spitch) and height > 0 and depth > 0
+    if depth > 1:
+        assert dslice % dpitch == 0 and sslice % spitch == 0
+        assert dslice >= dpitch * height and sslice >= spitch * height
     for z in range(depth):
         for y in range(height):
             d0, s0 = dst + z * dslice + y * dpitch, src + z * sslice + y * spitch
